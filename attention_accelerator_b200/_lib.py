@@ -1,0 +1,110 @@
+"""ctypes binding of ``include/gqa_b200.h`` (the library's C ABI).
+
+Loading fails loudly when ``lib/libgqa_b200.so`` is missing: there is no
+fallback implementation of any operation.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libgqa_b200.so"
+
+GQA_OK = 0
+GQA_ERR_GEOMETRY = 1
+GQA_ERR_SEQ_LEN = 2
+GQA_ERR_N_KV_TILES = 3
+GQA_ERR_SCALE = 4
+GQA_ERR_QUERY_POSITION = 5
+GQA_ERR_KV_BLOCK_LEN = 6
+GQA_ERR_GROUP_SIZE = 7
+GQA_ERR_NULL_POINTER = 8
+GQA_ERR_ALIGNMENT = 9
+GQA_ERR_WORKSPACE = 10
+GQA_ERR_BATCH = 11
+GQA_ERR_KV_RANGE = 12
+GQA_ERR_CUDA = 13
+GQA_ERR_DEVICE_TIMEOUT = 14
+GQA_ERR_UNSUPPORTED_DEVICE = 15
+GQA_ERR_ROPE_THETA = 16
+
+#: codes that describe a bad call configuration (the reference's config_error)
+CONFIG_ERRORS = {GQA_ERR_GEOMETRY, GQA_ERR_SEQ_LEN, GQA_ERR_N_KV_TILES, GQA_ERR_SCALE,
+                 GQA_ERR_QUERY_POSITION, GQA_ERR_KV_BLOCK_LEN, GQA_ERR_GROUP_SIZE,
+                 GQA_ERR_BATCH, GQA_ERR_KV_RANGE, GQA_ERR_ROPE_THETA}
+
+GQA_FLAG_PARTIAL_OUT = 0x1
+PARTIAL_FLOATS = 132
+
+
+class GqaParams(ctypes.Structure):
+    """Mirror of ``struct gqa_params``."""
+    _fields_ = [
+        ("n_q_heads", ctypes.c_uint32), ("n_kv_heads", ctypes.c_uint32),
+        ("head_dim", ctypes.c_uint32), ("tile_dim", ctypes.c_uint32),
+        ("seq_len", ctypes.c_uint32), ("n_kv_tiles", ctypes.c_uint32),
+        ("scale", ctypes.c_float), ("query_position", ctypes.c_uint32),
+        ("kv_block_len", ctypes.c_uint32), ("group_size", ctypes.c_uint32),
+        ("rope_theta", ctypes.c_float), ("flags", ctypes.c_uint32),
+        ("q_batch_stride", ctypes.c_int64), ("q_head_stride", ctypes.c_int64),
+        ("k_pos_stride", ctypes.c_int64), ("k_head_stride", ctypes.c_int64),
+        ("v_pos_stride", ctypes.c_int64), ("v_head_stride", ctypes.c_int64),
+        ("out_batch_stride", ctypes.c_int64), ("out_head_stride", ctypes.c_int64),
+        ("mask_out", ctypes.c_void_p), ("mask_stride", ctypes.c_int64),
+    ]
+
+
+class GqaSeqDesc(ctypes.Structure):
+    """Mirror of ``struct gqa_seq_desc`` (24 bytes)."""
+    _fields_ = [("kv_start", ctypes.c_int64), ("seq_len", ctypes.c_int32),
+                ("query_position", ctypes.c_int32), ("pos_begin", ctypes.c_int32),
+                ("pos_end", ctypes.c_int32)]
+
+
+_P = ctypes.c_void_p
+_SIGNATURES = {
+    "gqa_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "gqa_version": (ctypes.c_int, []),
+    "gqa_device_supported": (ctypes.c_int, [ctypes.c_int]),
+    "gqa_validate": (ctypes.c_int, [ctypes.POINTER(GqaParams)]),
+    "gqa_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(GqaParams), ctypes.POINTER(GqaSeqDesc), ctypes.c_int]),
+    "gqa_decode": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), _P, ctypes.c_size_t, _P]),
+    "gqa_decode_batched": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), ctypes.POINTER(GqaSeqDesc),
+                                          _P, ctypes.c_int, _P, ctypes.c_size_t, _P]),
+    "gqa_combine_partials": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _P,
+                                            ctypes.c_int64, ctypes.c_int64, _P]),
+    "gqa_rope_rows": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_float, _P]),
+    "gqa_rope_phase_rom": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, ctypes.c_double]),
+    "gqa_rope_sincos_rom": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
+    "gqa_read_status": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int)]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the CUDA library (once); raises if it has not been built."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.is_file():
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python -m attention_accelerator_b200.build` "
+                    "(there is no CPU implementation to fall back to)")
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return load().gqa_status_string(int(code)).decode()
+
+
+def exported_symbols() -> list[str]:
+    return sorted(_SIGNATURES)

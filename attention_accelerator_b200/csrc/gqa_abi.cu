@@ -1,0 +1,391 @@
+// gqa_abi.cu -- the extern "C" boundary declared in include/gqa_b200.h:
+// host-side validation (the reference's start-time config_error), planning of
+// key splits, workspace layout, argument packing and kernel launches.
+#include "gqa_b200.h"
+#include "gqa_device.cuh"
+#include "gqa_internal.h"
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+static_assert(sizeof(gqa_seq_desc) == sizeof(gqa::SeqDesc), "descriptor layout");
+static_assert(sizeof(gqa_partial_row) == gqa::kPartialFloats * sizeof(float), "partial row layout");
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr size_t kWsHeaderBytes = 256;
+constexpr int kMinChunk = 64;        // keys: one pipeline tile
+constexpr int kMinChunkMultiWave = 256;
+constexpr int kMaxWaves = 16;
+constexpr int kOverheadKeys = 64;    // per-CTA prologue/epilogue cost, in key-equivalents
+
+struct DeviceInfo {
+    bool init = false;
+    int status = GQA_OK;
+    int sms = 0;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+
+// Current device's SM count; prepares the kernels once per device.
+int current_device(int* sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GQA_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_mu);
+    DeviceInfo& di = g_dev[dev];
+    if (!di.init) {
+        int major = 0, minor = 0, n = 0;
+        if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            return GQA_ERR_CUDA;
+        }
+        if (major != 10 || minor != 0) {
+            di.status = GQA_ERR_UNSUPPORTED_DEVICE;
+        } else if (gqa::decode_prepare(dev) != cudaSuccess) {
+            di.status = GQA_ERR_CUDA;
+        }
+        di.sms = n;
+        di.init = true;
+    }
+    if (di.status != GQA_OK) return di.status;
+    *sms = di.sms;
+    return GQA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool stride_ok(int64_t s) { return s >= 0 && (s % 8) == 0; }
+
+int check_geometry(const gqa_params* p) {
+    if (p->n_q_heads != (uint32_t)gqa::kNumQHeads || p->n_kv_heads != (uint32_t)gqa::kNumKVHeads ||
+        p->head_dim != (uint32_t)gqa::kHeadDim || p->tile_dim != 16u)
+        return GQA_ERR_GEOMETRY;
+    if (p->kv_block_len == 0) return GQA_ERR_KV_BLOCK_LEN;
+    if (!(p->scale != 0.f) || !std::isfinite(p->scale)) return GQA_ERR_SCALE;
+    if (p->group_size != p->n_q_heads / p->n_kv_heads) return GQA_ERR_GROUP_SIZE;
+    if (!(p->rope_theta > 0.f) || !std::isfinite(p->rope_theta)) return GQA_ERR_ROPE_THETA;
+    return GQA_OK;
+}
+
+int check_layout(const void* q, const void* k, const void* v, const void* out, const gqa_params* p) {
+    if (!q || !k || !v || !out) return GQA_ERR_NULL_POINTER;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return GQA_ERR_ALIGNMENT;
+    if (!stride_ok(p->q_batch_stride) || !stride_ok(p->q_head_stride) || !stride_ok(p->k_head_stride) ||
+        !stride_ok(p->v_head_stride) || !stride_ok(p->k_pos_stride) || !stride_ok(p->v_pos_stride) ||
+        p->k_pos_stride == 0 || p->v_pos_stride == 0)
+        return GQA_ERR_ALIGNMENT;
+    if (p->flags & GQA_FLAG_PARTIAL_OUT) {
+        if (p->out_head_stride < gqa::kPartialFloats || p->out_head_stride % 4 || p->out_batch_stride < 0 ||
+            p->out_batch_stride % 4)
+            return GQA_ERR_ALIGNMENT;
+    } else if (p->out_head_stride < 0 || p->out_batch_stride < 0) {
+        return GQA_ERR_ALIGNMENT;
+    }
+    return GQA_OK;
+}
+
+int check_desc(const gqa::SeqDesc& d, bool need_keys) {
+    if (d.seq_len <= 0) return GQA_ERR_SEQ_LEN;
+    if (d.query_position < 0 || d.query_position >= d.seq_len) return GQA_ERR_QUERY_POSITION;
+    if (d.kv_start < 0 || d.pos_begin < 0 || d.pos_end < d.pos_begin || d.pos_end > d.seq_len)
+        return GQA_ERR_KV_RANGE;
+    if (need_keys && gqa::seq_key_count(d) == 0) return GQA_ERR_KV_RANGE;
+    return GQA_OK;
+}
+
+struct Plan {
+    int chunk = 0;
+    int total_splits = 0;
+    size_t off_counters = 0, off_partials = 0, ws_bytes = 0;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Keys per split: one wave of CTAs for a single sequence; for a batch, the
+// wave count (1..16) that minimises waves x (chunk + per-CTA overhead).
+Plan make_plan(const gqa::SeqDesc* d, int batch, int sms) {
+    const int slots = sms / gqa::kNumKVHeads > 0 ? sms / gqa::kNumKVHeads : 1;
+    int64_t total = 0;
+    for (int b = 0; b < batch; ++b) total += gqa::seq_key_count(d[b]);
+    auto splits_for = [&](int chunk) {
+        int64_t s = 0;
+        for (int b = 0; b < batch; ++b) s += gqa::seq_splits(d[b], chunk);
+        return s;
+    };
+    auto round8 = [](int64_t x) { return (int)(((x + 7) / 8) * 8); };
+    int best_chunk = 0;
+    double best_cost = 0;
+    const int max_w = batch == 1 ? 1 : kMaxWaves;
+    for (int w = 1; w <= max_w; ++w) {
+        int64_t chunk = (total + (int64_t)slots * w - 1) / ((int64_t)slots * w);
+        const int floor_chunk = (batch == 1 || w == 1) ? kMinChunk : kMinChunkMultiWave;
+        if (chunk < floor_chunk) chunk = floor_chunk;
+        const int c = round8(chunk);
+        const int64_t ctas = splits_for(c) * gqa::kNumKVHeads;
+        const int64_t waves = (ctas + sms - 1) / sms;
+        const double cost = (double)waves * (double)(c + kOverheadKeys);
+        if (best_chunk == 0 || cost < best_cost) {
+            best_chunk = c;
+            best_cost = cost;
+        }
+    }
+    Plan pl;
+    pl.chunk = best_chunk > 0 ? best_chunk : kMinChunk;
+    pl.total_splits = (int)splits_for(pl.chunk);
+    pl.off_counters = kWsHeaderBytes;
+    pl.off_partials = pl.off_counters + align256((size_t)batch * gqa::kNumKVHeads * sizeof(uint32_t));
+    pl.ws_bytes = pl.off_partials + (size_t)pl.total_splits * gqa::kNumKVHeads * gqa::kGroup *
+                                        gqa::kPartialFloats * sizeof(float);
+    return pl;
+}
+
+void rope_steps(double theta, uint64_t* step, float2* rot_step, float2* rot_tile, int tile_keys) {
+    const double two_pi = 2.0 * M_PI;
+    for (int i = 0; i < gqa::kPairs; ++i) {
+        const double inv = std::pow(theta, -2.0 * i / (double)gqa::kHeadDim);
+        const double turns_q64 = inv / two_pi * 18446744073709551616.0;  // < 2^62
+        step[i] = (uint64_t)std::llround(turns_q64);
+        if (rot_step) rot_step[i] = make_float2((float)std::cos(4.0 * inv), (float)std::sin(4.0 * inv));
+        if (rot_tile)
+            rot_tile[i] = make_float2((float)std::cos(tile_keys * inv), (float)std::sin(tile_keys * inv));
+    }
+}
+
+gqa::SeqDesc single_desc(const gqa_params* p) {
+    gqa::SeqDesc d;
+    d.kv_start = 0;
+    d.seq_len = (int32_t)p->seq_len;
+    d.query_position = (int32_t)p->query_position;
+    d.pos_begin = 0;
+    d.pos_end = (int32_t)p->seq_len;
+    return d;
+}
+
+void fill_args(gqa::DecodeArgs& a, const void* q, const void* k, const void* v, void* out, const gqa_params* p,
+               void* ws, const Plan& pl, int batch) {
+    std::memset(&a, 0, sizeof(a));
+    a.q = static_cast<const __nv_bfloat16*>(q);
+    a.k = static_cast<const __nv_bfloat16*>(k);
+    a.v = static_cast<const __nv_bfloat16*>(v);
+    a.out = out;
+    a.q_bstride = p->q_batch_stride;
+    a.q_hstride = p->q_head_stride;
+    a.k_pstride = p->k_pos_stride;
+    a.k_hstride = p->k_head_stride;
+    a.v_pstride = p->v_pos_stride;
+    a.v_hstride = p->v_head_stride;
+    a.o_bstride = p->out_batch_stride;
+    a.o_hstride = p->out_head_stride;
+    a.batch = batch;
+    a.chunk = pl.chunk;
+    a.qscale = (float)((double)p->scale * 1.4426950408889634);
+    a.flags = p->flags;
+    uint8_t* w = static_cast<uint8_t*>(ws);
+    a.ws_status = reinterpret_cast<uint32_t*>(w);
+    a.ws_counters = reinterpret_cast<uint32_t*>(w + pl.off_counters);
+    a.ws_partials = reinterpret_cast<float*>(w + pl.off_partials);
+    a.mask_out = p->mask_out;
+    a.mask_stride = p->mask_stride;
+    a.kv_block_len = (int)p->kv_block_len;
+    rope_steps((double)p->rope_theta, a.rope_step, a.rot_step, a.rot_tile, gqa::decode_tile_keys());
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gqa_status_string(int status) {
+    switch (status) {
+        case GQA_OK: return "ok";
+        case GQA_ERR_GEOMETRY: return "invalid configuration: N_Q_HEADS/N_KV_HEADS/HEAD_DIM/TILE_DIM must be 32/8/128/16";
+        case GQA_ERR_SEQ_LEN: return "invalid configuration: SEQ_LEN must be positive";
+        case GQA_ERR_N_KV_TILES: return "invalid configuration: N_KV_TILES must equal ceil(SEQ_LEN / KV_BLOCK_LEN)";
+        case GQA_ERR_SCALE: return "invalid configuration: SCALE_FACTOR must be non-zero and finite";
+        case GQA_ERR_QUERY_POSITION: return "invalid configuration: QUERY_POSITION must be in [0, SEQ_LEN)";
+        case GQA_ERR_KV_BLOCK_LEN: return "invalid configuration: KV_BLOCK_LEN must be positive";
+        case GQA_ERR_GROUP_SIZE: return "invalid configuration: GROUP_SIZE must equal N_Q_HEADS / N_KV_HEADS";
+        case GQA_ERR_NULL_POINTER: return "null tensor pointer";
+        case GQA_ERR_ALIGNMENT: return "tensor pointer not 16-byte aligned or stride not a multiple of 8 elements";
+        case GQA_ERR_WORKSPACE: return "workspace missing or too small";
+        case GQA_ERR_BATCH: return "invalid batch or sequence descriptor";
+        case GQA_ERR_KV_RANGE: return "invalid stored key range";
+        case GQA_ERR_CUDA: return "CUDA runtime error";
+        case GQA_ERR_DEVICE_TIMEOUT: return "a bounded wait inside a kernel timed out";
+        case GQA_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 GPU";
+        case GQA_ERR_ROPE_THETA: return "invalid rope_theta";
+        default: return "unknown status";
+    }
+}
+
+int gqa_version(void) { return (0 << 16) | (1 << 8) | 0; }
+
+int gqa_device_supported(int device) {
+    int major = 0, minor = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device) != cudaSuccess) return 0;
+    return major == 10 && minor == 0;
+}
+
+int gqa_validate(const gqa_params* p) {
+    if (!p) return GQA_ERR_NULL_POINTER;
+    // Same conditions, same order, as config_error (gqa_attention_wrapper.v:230-237),
+    // then the generator's QUERY_POSITION range (gen_gqa_wrapper_vectors.py:77-78).
+    if (p->n_q_heads != (uint32_t)gqa::kNumQHeads || p->n_kv_heads != (uint32_t)gqa::kNumKVHeads ||
+        p->head_dim != (uint32_t)gqa::kHeadDim || p->tile_dim != 16u)
+        return GQA_ERR_GEOMETRY;
+    if (p->seq_len == 0) return GQA_ERR_SEQ_LEN;
+    if (p->kv_block_len == 0) return GQA_ERR_KV_BLOCK_LEN;
+    if (p->n_kv_tiles != (p->seq_len + p->kv_block_len - 1) / p->kv_block_len) return GQA_ERR_N_KV_TILES;
+    if (p->seq_len > 0x7FFFFFFFu) return GQA_ERR_SEQ_LEN;
+    const int g = check_geometry(p);
+    if (g != GQA_OK) return g;
+    if (p->query_position >= p->seq_len) return GQA_ERR_QUERY_POSITION;
+    return GQA_OK;
+}
+
+size_t gqa_workspace_bytes(const gqa_params* p, const gqa_seq_desc* descs, int batch) {
+    if (!p) return 0;
+    int sms = 0;
+    if (current_device(&sms) != GQA_OK) return 0;
+    if (descs == nullptr) {
+        if (batch != 1 || gqa_validate(p) != GQA_OK) return 0;
+        const gqa::SeqDesc d = single_desc(p);
+        return make_plan(&d, 1, sms).ws_bytes;
+    }
+    if (batch < 1) return 0;
+    const gqa::SeqDesc* d = reinterpret_cast<const gqa::SeqDesc*>(descs);
+    for (int b = 0; b < batch; ++b)
+        if (check_desc(d[b], false) != GQA_OK) return 0;
+    return make_plan(d, batch, sms).ws_bytes;
+}
+
+int gqa_decode(const void* q, const void* k, const void* v, void* out, const gqa_params* p, void* workspace,
+               size_t workspace_bytes, void* stream) {
+    int st = gqa_validate(p);
+    if (st != GQA_OK) return st;
+    st = check_layout(q, k, v, out, p);
+    if (st != GQA_OK) return st;
+    int sms = 0;
+    st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    const gqa::SeqDesc d = single_desc(p);
+    const Plan pl = make_plan(&d, 1, sms);
+    if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
+    gqa::DecodeArgs a;
+    fill_args(a, q, k, v, out, p, workspace, pl, 1);
+    a.descs = nullptr;
+    a.single = d;
+    if (gqa::launch_decode(a, pl.total_splits * gqa::kNumKVHeads, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return GQA_ERR_CUDA;
+    return GQA_OK;
+}
+
+int gqa_decode_batched(const void* q, const void* k, const void* v, void* out, const gqa_params* p,
+                       const gqa_seq_desc* host_descs, const gqa_seq_desc* dev_descs, int batch, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+    if (!p) return GQA_ERR_NULL_POINTER;
+    int st = check_geometry(p);
+    if (st != GQA_OK) return st;
+    if (batch < 1) return GQA_ERR_BATCH;
+    if (!host_descs || !dev_descs) return GQA_ERR_NULL_POINTER;
+    st = check_layout(q, k, v, out, p);
+    if (st != GQA_OK) return st;
+    const gqa::SeqDesc* d = reinterpret_cast<const gqa::SeqDesc*>(host_descs);
+    const bool need_keys = (p->flags & GQA_FLAG_PARTIAL_OUT) == 0;
+    for (int b = 0; b < batch; ++b) {
+        st = check_desc(d[b], need_keys);
+        if (st != GQA_OK) return st;
+    }
+    int sms = 0;
+    st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    const Plan pl = make_plan(d, batch, sms);
+    if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
+    gqa::DecodeArgs a;
+    fill_args(a, q, k, v, out, p, workspace, pl, batch);
+    a.descs = reinterpret_cast<const gqa::SeqDesc*>(dev_descs);
+    a.single = d[0];
+    if (gqa::launch_decode(a, pl.total_splits * gqa::kNumKVHeads, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return GQA_ERR_CUDA;
+    return GQA_OK;
+}
+
+int gqa_combine_partials(const float* partials, int n_parts, int64_t part_stride, int64_t batch_stride, int batch,
+                         void* out, int64_t out_batch_stride, int64_t out_head_stride, void* stream) {
+    if (!partials || !out) return GQA_ERR_NULL_POINTER;
+    if (n_parts < 1 || batch < 1) return GQA_ERR_BATCH;
+    if (part_stride < 0 || batch_stride < 0 || out_batch_stride < 0 || out_head_stride < 0) return GQA_ERR_ALIGNMENT;
+    int sms = 0;
+    const int st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    if (gqa::launch_combine(partials, n_parts, part_stride, batch_stride, batch, out, out_batch_stride,
+                            out_head_stride, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return GQA_ERR_CUDA;
+    return GQA_OK;
+}
+
+int gqa_rope_rows(const void* x, const int32_t* positions, float* out, int rows, float rope_theta, void* stream) {
+    if (!x || !positions || !out) return GQA_ERR_NULL_POINTER;
+    if (rows < 0) return GQA_ERR_BATCH;
+    if (!(rope_theta > 0.f) || !std::isfinite(rope_theta)) return GQA_ERR_ROPE_THETA;
+    if (rows == 0) return GQA_OK;
+    int sms = 0;
+    const int st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    uint64_t step[gqa::kPairs];
+    rope_steps((double)rope_theta, step, nullptr, nullptr, 0);
+    if (gqa::launch_rope_rows(x, positions, out, rows, step, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return GQA_ERR_CUDA;
+    return GQA_OK;
+}
+
+int gqa_rope_phase_rom(uint32_t* phase, int head_dim, double rope_theta) {
+    if (!phase) return GQA_ERR_NULL_POINTER;
+    if (head_dim <= 0 || head_dim % 2) return GQA_ERR_GEOMETRY;
+    if (!(rope_theta > 0.0) || !std::isfinite(rope_theta)) return GQA_ERR_ROPE_THETA;
+    const int pairs = head_dim / 2;
+    for (int i = 0; i < pairs; ++i) {
+        // tools/gen_rope_rom.py:45-47: round(inv_freq * 2**32 / (2*pi)) mod 2**32,
+        // Python's round() being round-half-even like nearbyint().
+        const double inv = std::pow(rope_theta, -(double)i / pairs);
+        const double v = std::nearbyint(inv * 4294967296.0 / (2.0 * M_PI));
+        phase[i] = (uint32_t)((uint64_t)v & 0xFFFFFFFFull);
+    }
+    return GQA_OK;
+}
+
+static uint32_t f32_to_bf16_bits(double x) {
+    const float f = (float)x;
+    uint32_t bits;
+    std::memcpy(&bits, &f, 4);
+    const uint32_t lsb = (bits >> 16) & 1u;
+    return (uint32_t)((((uint64_t)bits + 0x7FFFu + lsb) >> 16) & 0xFFFFu);
+}
+
+int gqa_rope_sincos_rom(uint32_t* sincos, int addr_bits) {
+    if (!sincos) return GQA_ERR_NULL_POINTER;
+    if (addr_bits < 1 || addr_bits > 24) return GQA_ERR_GEOMETRY;
+    const int n = 1 << addr_bits;
+    for (int i = 0; i < n; ++i) {
+        // tools/gen_rope_rom.py:49-54: angle = 2*pi*i/N, {bf16(cos), bf16(sin)}.
+        const double a = 2.0 * M_PI * (double)i / (double)n;
+        sincos[i] = (f32_to_bf16_bits(std::cos(a)) << 16) | f32_to_bf16_bits(std::sin(a));
+    }
+    return GQA_OK;
+}
+
+int gqa_read_status(void* workspace, void* stream, int* device_status) {
+    if (!workspace || !device_status) return GQA_ERR_NULL_POINTER;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint32_t v = 0;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return GQA_ERR_CUDA;
+    if (cudaMemcpy(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return GQA_ERR_CUDA;
+    if (v != 0 && cudaMemset(workspace, 0, sizeof(v)) != cudaSuccess) return GQA_ERR_CUDA;
+    *device_status = v ? GQA_ERR_DEVICE_TIMEOUT : GQA_OK;
+    return GQA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,195 @@
+// gqa_device.cuh -- device-side building blocks shared by the sm_100a kernels:
+// geometry constants, the kernel argument block, mbarrier / bulk-copy PTX
+// wrappers with bounded waits, BF16 unpacking and the RoPE phase generator.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace gqa {
+
+// Llama-3-8B GQA geometry the reference RTL is fixed to
+// (gqa_attention_wrapper.v:47-68, axi_lite_regs.v:108-117).
+constexpr int kHeadDim = 128;
+constexpr int kPairs = kHeadDim / 2;   // rotate_half pairs (i, i+64)
+constexpr int kNumQHeads = 32;
+constexpr int kNumKVHeads = 8;
+constexpr int kGroup = kNumQHeads / kNumKVHeads;
+constexpr int kRowBytes = kHeadDim * 2;  // one BF16 K or V row
+constexpr int kPartialFloats = 132;      // gqa_partial_row: acc[128], m, l, pad[2]
+
+// Device status word values (first word of the workspace).
+constexpr uint32_t kDevStatusTimeout = 1u;
+
+// A bounded wait gives up after this many SM clock cycles (~1 s at 1.9 GHz).
+constexpr long long kWaitTimeoutCycles = 2000000000LL;
+
+struct SeqDesc {  // layout-identical to gqa_seq_desc
+    int64_t kv_start;
+    int32_t seq_len;
+    int32_t query_position;
+    int32_t pos_begin;
+    int32_t pos_end;
+};
+
+// Keys a call reads for one sequence: [pos_begin, min(pos_end, n_vis)) with
+// n_vis = min(seq_len, query_position + 1), i.e. the positions the hardware
+// mask (gqa_attention_wrapper.v:279) lets through.
+__host__ __device__ inline int seq_key_begin(const SeqDesc& d) { return d.pos_begin; }
+__host__ __device__ inline int seq_key_count(const SeqDesc& d) {
+    int n_vis = d.seq_len < d.query_position + 1 ? d.seq_len : d.query_position + 1;
+    int hi = d.pos_end < n_vis ? d.pos_end : n_vis;
+    int n = hi - d.pos_begin;
+    return n > 0 ? n : 0;
+}
+__host__ __device__ inline int seq_splits(const SeqDesc& d, int chunk) {
+    int n = seq_key_count(d);
+    int s = (n + chunk - 1) / chunk;
+    return s > 0 ? s : 1;
+}
+
+// key_valid of gqa_attention_wrapper.v:279 / score_tag_fifo push_key_valid.
+__host__ __device__ inline bool key_valid(int64_t p, int seq_len, int query_position) {
+    return p < seq_len && p <= query_position;
+}
+
+struct DecodeArgs {
+    const __nv_bfloat16* q;
+    const __nv_bfloat16* k;
+    const __nv_bfloat16* v;
+    void* out;
+    int64_t q_bstride, q_hstride;
+    int64_t k_pstride, k_hstride;
+    int64_t v_pstride, v_hstride;
+    int64_t o_bstride, o_hstride;
+    const SeqDesc* descs;   // device array, or nullptr: use `single`
+    SeqDesc single;
+    int batch;
+    int chunk;              // keys per split
+    float qscale;           // scale * log2(e): scores are kept in log2 units
+    uint32_t flags;         // GQA_FLAG_*
+    uint32_t* ws_status;
+    uint32_t* ws_counters;  // [batch][8] split counters, self-resetting
+    float* ws_partials;     // [total_splits][8][4][132]
+    uint8_t* mask_out;
+    int64_t mask_stride;
+    int kv_block_len;
+    uint64_t rope_step[kPairs];  // Q0.64 turns per position for each pair
+    float2 rot_step[kPairs];     // e^{i*theta_i*4}: advance of 4 positions
+    float2 rot_tile[kPairs];     // e^{i*theta_i*TP}: advance of one pipeline tile
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase with parity `parity` to complete; false after the timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitTimeoutCycles) return false;
+    }
+    return true;
+}
+
+// L2 policy for streamed-once K/V rows.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// Bulk (non-tensor) TMA copy global -> this CTA's shared memory, completing
+// `bytes` of transaction count on `bar`.  16-byte aligned addresses, size a
+// multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                          uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "r"(smem_addr(p)));
+    return r;
+}
+
+__device__ __forceinline__ uint2 lds64(const void* p) {
+    uint2 r;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(smem_addr(p)));
+    return r;
+}
+
+__device__ __forceinline__ float4 lds128f(const void* p) {
+    float4 r;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "r"(smem_addr(p)));
+    return r;
+}
+
+// Two BF16 codes in one 32-bit word -> (element 2j, element 2j+1) as float2.
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+// ---------------------------------------------------------------------------
+// RoPE phase.  Pair i turns by theta^(-2i/128) / (2*pi) turns per position,
+// held as an unsigned Q0.64 fraction: the product with a position wraps
+// modulo one turn exactly.  This is the numerically-controlled-oscillator idea
+// of rope_unit.v:159-172 with a 64-bit phase, followed by sincospif on the
+// reduced angle instead of a 14-bit BF16 ROM.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 rope_factor(uint64_t step, int64_t pos) {
+    const uint64_t ph = step * static_cast<uint64_t>(pos);
+    const float x = __ll2float_rn(static_cast<long long>(ph)) * 0x1p-63f;  // 2*turns in [-1, 1)
+    float s, c;
+    sincospif(x, &s, &c);
+    return make_float2(c, s);
+}
+
+}  // namespace gqa

@@ -1,0 +1,111 @@
+"""Drop-in for the ``$VIVADO`` executable that ``pyfiles/run_gqa_regression.py`` runs.
+
+The regression driver calls ``$VIVADO -mode batch -source
+scripts/run_gqa_wrapper_sim.tcl`` (run_gqa_regression.py:36,57,70) with
+``VECTORS_DIR`` and ``SIM_BUILD_DIR`` in the environment, optionally
+``OUTPUT_BACKPRESSURE`` or ``INVALID_CONFIG``, and passes a case when the exit
+status is 0 and stdout contains ``PASS:`` (:59, :72).  This program keeps that
+contract with the B200 library in place of the XSim testbench:
+
+* reads ``gqa_{q,k,v,golden}.mem`` and ``gqa_config.txt`` from VECTORS_DIR
+  (run_gqa_wrapper_sim.tcl:13-27);
+* programs the registers as the testbench does (tb_gqa_attention_wrapper.sv:323-329),
+  taking QUERY_POSITION and KV_BLOCK_LEN from the config, and the exact
+  1/sqrt(128) scale of the golden;
+* runs one decode through ``gqa_decode`` on the GPU, writes the rows to
+  ``SIM_BUILD_DIR/gqa_rtl_out.mem`` (one 128-element row per line, the
+  testbench's ``$fdisplay`` format), checks every element against the golden
+  with the checker's rule (<= MAX_ULP, default 64, with the 0x3d exponent
+  exemption) and prints ``PASS:``/``FAIL:``;
+* with INVALID_CONFIG, programs N_Q_HEADS=31 (tb :323) and passes only if the
+  library rejects the start (tb :330-336).
+OUTPUT_BACKPRESSURE only throttles the RTL's AXIS egress; it has no GPU meaning
+and is accepted and ignored.
+"""
+from __future__ import annotations
+
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+
+def _fail(msg: str, code: int = 1) -> int:
+    print(f"ERROR: {msg}")
+    return code
+
+
+def main(argv: list[str] | None = None) -> int:
+    from . import _lib
+    from .api import GqaConfigError, make_params
+    from .memfile import compare_rows, read_config, read_mem, write_mem
+
+    vectors = Path(os.environ.get("VECTORS_DIR") or "tests/data").resolve()
+    build = Path(os.environ.get("SIM_BUILD_DIR") or "build/gqa_wrapper_sim").resolve()
+    max_ulp = int(os.environ.get("MAX_ULP", "64"))
+    for req in ("gqa_q.mem", "gqa_k.mem", "gqa_v.mem", "gqa_golden.mem"):
+        if not (vectors / req).is_file():
+            return _fail(f"Missing {vectors / req}.")
+    if not (vectors / "gqa_config.txt").is_file():
+        return _fail(f"Missing {vectors / 'gqa_config.txt'}.")
+    cfg = read_config(vectors / "gqa_config.txt")
+    if "SEQ_LEN" not in cfg:
+        return _fail("SEQ_LEN missing from gqa_config.txt")
+    seq_len = int(cfg["SEQ_LEN"])
+    kv_block_len = int(cfg.get("KV_BLOCK_LEN", 16))
+    qpos = int(cfg.get("QUERY_POSITION", seq_len - 1))
+    build.mkdir(parents=True, exist_ok=True)
+    out_path = build / "gqa_rtl_out.mem"
+
+    if os.environ.get("INVALID_CONFIG"):
+        # N_Q_HEADS = 31 with everything else as in the testbench, then START.
+        p = make_params(seq_len=seq_len, query_position=qpos, kv_block_len=kv_block_len, n_q_heads=31)
+        lib = _lib.load()
+        import ctypes
+        status = lib.gqa_decode(None, None, None, None, ctypes.byref(p), None, 0, None)
+        out_path.write_text("")
+        if status in _lib.CONFIG_ERRORS:
+            print(f"config_error: {_lib.status_string(status)}")
+            print("PASS: invalid configuration rejected")
+            return 0
+        print(f"FAIL: invalid configuration was not rejected (status {status})")
+        return 1
+
+    import torch
+    from .api import decode
+    if not torch.cuda.is_available():
+        return _fail("no CUDA device: the B200 library has no CPU path")
+    q = read_mem(vectors / "gqa_q.mem", 16).reshape(-1, 128)
+    k = read_mem(vectors / "gqa_k.mem", 16).reshape(8, -1, 128)
+    v = read_mem(vectors / "gqa_v.mem", 16).reshape(8, -1, 128)
+    golden = read_mem(vectors / "gqa_golden.mem", 128)
+    dev = torch.device("cuda", torch.cuda.current_device())
+
+    def to_dev(a):
+        return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16).to(dev)
+
+    try:
+        out = decode(to_dev(q), to_dev(k), to_dev(v), seq_len=seq_len, query_position=qpos,
+                     kv_block_len=kv_block_len, layout="head_major")
+    except GqaConfigError as exc:
+        print(f"FAIL: configuration rejected: {exc}")
+        return 1
+    rows = out.view(torch.int16).cpu().numpy().astype(np.uint16)
+    write_mem(out_path, rows)
+    if golden.shape != rows.shape:
+        print(f"FAIL: golden has {golden.shape[0]} rows, output has {rows.shape[0]}")
+        return 1
+    res = compare_rows(golden, rows, max_ulp)
+    if res["failures"]:
+        print(f"FAIL: {res['failures']} elements exceeded {max_ulp} ULP; worst={res['worst']} "
+              f"at row={res['worst_row']}, col={res['worst_col']}")
+        return 1
+    print(f"PASS: {rows.shape[0]} GQA output rows matched golden within {max_ulp} ULP "
+          f"(worst ULP={res['worst']} at row={res['worst_row']}, col={res['worst_col']}; "
+          f"mean ULP={res['mean']:.4f}); output {out_path}")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main(sys.argv[1:]))

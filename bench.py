@@ -1,0 +1,583 @@
+#!/usr/bin/env python3
+"""Benchmark of the GQA decode-attention hot path (BASELINE metric: decode-attn
+KV-read HBM GB/s, % of the measured HBM peak, and query-heads/s, at 1/2/4/8 B200).
+
+One step = one pass of the hot path over one batch of synthetic input:
+  config2 (default): one single-token decode, SEQ_LEN=4096, QUERY_POSITION=4095,
+                     position-major BF16 KV cache [4096, 8, 128] per GPU.
+  config1:           SEQ_LEN=30, QUERY_POSITION=29, KV_BLOCK_LEN=16, U[-1,1) inputs.
+  config3:           batch 64, SEQ_LEN ~ U{512..8192}, K with log-normal channel scales.
+  config4:           SEQ_LEN=131072; at N>1 GPUs the sequence is split into
+                     contiguous shards, FP32 partials are all-gathered over NCCL and
+                     merged by the LSE combine kernel (strong scaling).
+Configs 1-3 shard by sequence: every rank decodes its own sequences, no
+collective (weak scaling).
+
+Timing: K steps replayed from CUDA graphs on one stream between CUDA events,
+after W warm-up steps, barrier + synchronize on both sides, max over ranks.
+Inputs rotate over buffer sets whose total exceeds twice the L2 size, so every
+step reads K/V from HBM.  ``--impl reference`` times the CPU restatement of the
+reference golden (the reference itself is Python that cannot run on the GPU box)
+on all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode-attn KV-read HBM GB/s (% of peak) + query-heads/sec at 1/2/4/8 B200"
+UNIT = "GB/s"
+FALLBACK_HBM_GBS = 6650.0
+L2_BYTES = 126 * 1024 * 1024
+HEAD_BYTES = 32 * 128 * 2
+
+
+def kv_bytes(n_keys: int) -> int:
+    """Algorithmic bytes of one sequence's decode: K+V rows of the visible keys, Q and out."""
+    return 2 * n_keys * 8 * 128 * 2 + 2 * HEAD_BYTES
+
+
+def peak_hbm():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples taken while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.rows, self.window = [], None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.monotonic(), [x.strip() for x in line.split(",")]))
+
+    def mark(self, start: float, end: float):
+        self.window = (start, end)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = self.rows
+        if self.window:
+            inside = [r for t, r in rows if self.window[0] - 0.06 <= t <= self.window[1] + 0.06]
+            rows = inside if inside else [r for _, r in rows]
+        else:
+            rows = [r for _, r in rows]
+        sm = [float(r[1]) for r in rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows if len(r) > 8 for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+class Workload:
+    name = ""
+    scaling = "weak"
+    launches_per_step = 1
+
+    def launch(self, i: int):
+        raise NotImplementedError
+
+    @property
+    def sets(self) -> int:
+        return 1
+
+
+class SingleDecode(Workload):
+    """One sequence per step per GPU; rotating buffer sets beat the L2."""
+
+    def __init__(self, device, rank, seq_len, qpos, uniform=False, seed=20260805):
+        import torch
+        import attention_accelerator_b200 as gqa
+        self.gqa, self.torch = gqa, torch
+        self.S, self.qpos = seq_len, qpos
+        self.name = f"config1_decode_s{seq_len}" if uniform else f"config2_decode_s{seq_len}"
+        self.bytes_per_step = kv_bytes(qpos + 1)
+        self.qheads_per_step = 32
+        per_set = 2 * seq_len * 8 * 128 * 2
+        self.nsets = max(2, math.ceil(2 * L2_BYTES / per_set)) if per_set < 2 * L2_BYTES else 2
+        self.nsets = min(self.nsets, 64)
+        g = torch.Generator(device=device).manual_seed(seed + 7919 * rank)
+
+        def rnd(shape):
+            if uniform:
+                return (torch.rand(shape, generator=g, device=device) * 2 - 1).to(torch.bfloat16)
+            return torch.randn(shape, generator=g, device=device).to(torch.bfloat16)
+
+        self.q = [rnd((32, 128)) for _ in range(self.nsets)]
+        self.k = [rnd((seq_len, 8, 128)) for _ in range(self.nsets)]
+        self.v = [rnd((seq_len, 8, 128)) for _ in range(self.nsets)]
+        self.out = torch.empty((32, 128), dtype=torch.bfloat16, device=device)
+        self.l2_note = (f"{self.nsets} rotating buffer sets of {per_set / 2**20:.1f} MiB "
+                        f"({self.nsets * per_set / 2**20:.0f} MiB > 2x L2)")
+
+    @property
+    def sets(self):
+        return self.nsets
+
+    def launch(self, i):
+        j = i % self.nsets
+        self.gqa.decode(self.q[j], self.k[j], self.v[j], seq_len=self.S, query_position=self.qpos, out=self.out)
+
+    def config(self):
+        return {"workload": self.name, "batch_per_gpu": 1, "seq_len": self.S, "query_position": self.qpos,
+                "kv_block_len": 16, "kv_layout": "position_major [S,8,128] bf16", "l2": self.l2_note}
+
+    def e2e_inputs(self):
+        t = self.torch
+        return [x.cpu().pin_memory() for x in (self.q[0], self.k[0], self.v[0])]
+
+    def e2e_step(self, host):
+        q, k, v = host
+        return self.gqa.decode(q, k, v, seq_len=self.S, query_position=self.qpos)
+
+    def oracle_inputs(self):
+        """Head-major BF16 codes of buffer set 0 for the CPU restatement."""
+        import numpy as np
+        t = self.torch
+
+        def bits(x):
+            return x.contiguous().view(t.int16).cpu().numpy().astype(np.uint16)
+        return (bits(self.q[0]), bits(self.k[0].transpose(0, 1)), bits(self.v[0].transpose(0, 1)),
+                self.S, self.qpos)
+
+    def gpu_result_set0(self):
+        import numpy as np
+        self.launch(0)
+        self.torch.cuda.synchronize()
+        return self.out.view(self.torch.int16).cpu().numpy().astype(np.uint16)
+
+
+class RaggedBatch(Workload):
+    """64 sequences, SEQ_LEN ~ U{512..8192}, K with outlier channels."""
+
+    def __init__(self, device, rank, batch=64, seed=20260805):
+        import numpy as np
+        import torch
+        import attention_accelerator_b200 as gqa
+        self.gqa, self.torch = gqa, torch
+        rng = np.random.default_rng(seed + rank)
+        self.seq = [int(x) for x in rng.integers(512, 8193, size=batch)]
+        self.batch = batch
+        self.name = "config3_ragged_b64"
+        total = sum(self.seq)
+        self.bytes_per_step = sum(kv_bytes(s) for s in self.seq)
+        self.qheads_per_step = 32 * batch
+        per_set = 2 * total * 8 * 128 * 2
+        self.nsets = max(2, math.ceil(2 * L2_BYTES / per_set))
+        g = torch.Generator(device=device).manual_seed(seed + 7919 * rank)
+        scale = torch.exp(torch.randn((1, 8, 128), generator=g, device=device))
+        self.q = [torch.randn((batch, 32, 128), generator=g, device=device).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.k = [(torch.randn((total, 8, 128), generator=g, device=device) * scale).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.v = [torch.randn((total, 8, 128), generator=g, device=device).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.plan = gqa.plan_batch(self.seq, device=device)
+        self.out = torch.empty((batch, 32, 128), dtype=torch.bfloat16, device=device)
+        self.l2_note = f"{self.nsets} rotating buffer sets of {per_set / 2**20:.0f} MiB"
+
+    @property
+    def sets(self):
+        return self.nsets
+
+    def launch(self, i):
+        j = i % self.nsets
+        self.gqa.decode_batch(self.q[j], self.k[j], self.v[j], self.plan, out=self.out)
+
+    def config(self):
+        return {"workload": self.name, "batch_per_gpu": self.batch, "seq_len": "U{512..8192} seeded",
+                "total_keys": sum(self.seq), "kv_layout": "packed position_major [sum S,8,128] bf16",
+                "k_channel_scale": "exp(N(0,1)) per (kv head, dim)", "l2": self.l2_note}
+
+    def e2e_inputs(self):
+        return [x.cpu().pin_memory() for x in (self.q[0], self.k[0], self.v[0])]
+
+    def e2e_step(self, host):
+        t = self.torch
+        dev = self.out.device
+        q, k, v = (x.to(dev, non_blocking=True) for x in host)
+        out = self.gqa.decode_batch(q, k, v, self.plan)
+        return out.cpu()
+
+    def oracle_inputs(self):
+        return None
+
+    def gpu_result_set0(self):
+        return None
+
+
+class LongContext(Workload):
+    """SEQ_LEN=131072; contiguous key shards across ranks + NCCL all-gather."""
+
+    def __init__(self, device, rank, world, seq_len=131072, seed=20260805):
+        import torch
+        import attention_accelerator_b200 as gqa
+        self.gqa, self.torch = gqa, torch
+        self.rank, self.world = rank, world
+        self.S = seq_len
+        self.name = f"config4_decode_s{seq_len}"
+        self.scaling = "strong"
+        self.bytes_per_step = kv_bytes(seq_len)  # whole job; each rank reads 1/world of the keys
+        self.qheads_per_step = 32
+        lo, hi = rank * seq_len // world, (rank + 1) * seq_len // world
+        self.lo, self.hi = lo, hi
+        per_set = 2 * (hi - lo) * 8 * 128 * 2
+        self.nsets = max(2, math.ceil(2 * L2_BYTES / per_set))
+        g = torch.Generator(device=device).manual_seed(seed)  # same Q on all ranks
+        self.q = [torch.randn((1, 32, 128), generator=g, device=device).to(torch.bfloat16) for _ in range(self.nsets)]
+        self.k = [torch.randn((hi - lo, 8, 128), generator=g, device=device).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.v = [torch.randn((hi - lo, 8, 128), generator=g, device=device).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.device = device
+        if world == 1:
+            self.out = torch.empty((32, 128), dtype=torch.bfloat16, device=device)
+        else:
+            self.plan = gqa.plan_batch([seq_len], pos_begin=[lo], pos_end=[hi], kv_starts=[0], partial=True,
+                                       device=device)
+            self.part = torch.empty((1, 32, 132), dtype=torch.float32, device=device)
+            self.gathered = torch.empty((world, 1, 32, 132), dtype=torch.float32, device=device)
+            self.out = torch.empty((1, 32, 128), dtype=torch.bfloat16, device=device)
+            self.launches_per_step = 2
+        self.l2_note = f"{self.nsets} rotating buffer sets of {per_set / 2**20:.0f} MiB per rank"
+
+    @property
+    def sets(self):
+        return self.nsets
+
+    def launch(self, i):
+        j = i % self.nsets
+        if self.world == 1:
+            self.gqa.decode(self.q[j][0], self.k[j], self.v[j], seq_len=self.S, query_position=self.S - 1,
+                            out=self.out)
+            return
+        import torch.distributed as dist
+        self.gqa.decode_batch(self.q[j], self.k[j], self.v[j], self.plan, out=self.part)
+        dist.all_gather_into_tensor(self.gathered.view(self.world, -1), self.part.view(-1))
+        self.gqa.combine_partials(self.gathered, out=self.out)
+
+    def config(self):
+        return {"workload": self.name, "batch": 1, "seq_len": self.S, "query_position": self.S - 1,
+                "kv_layout": "position_major shard [S/N,8,128] bf16 per GPU",
+                "parallelism": f"sequence split x{self.world}, NCCL all-gather of 32x132 FP32 partials"
+                if self.world > 1 else "single GPU", "l2": self.l2_note}
+
+    def e2e_inputs(self):
+        return [x.cpu().pin_memory() for x in (self.q[0], self.k[0], self.v[0])]
+
+    def e2e_step(self, host):
+        dev = self.device
+        q, k, v = (x.to(dev, non_blocking=True) for x in host)
+        if self.world == 1:
+            out = self.gqa.decode(q[0], k, v, seq_len=self.S, query_position=self.S - 1)
+        else:
+            import torch.distributed as dist
+            part = self.gqa.decode_batch(q, k, v, self.plan)
+            gathered = self.torch.empty((self.world,) + tuple(part.shape), dtype=part.dtype, device=dev)
+            dist.all_gather_into_tensor(gathered.view(self.world, -1), part.view(-1))
+            out = self.gqa.combine_partials(gathered)
+        return out.cpu()
+
+    def oracle_inputs(self):
+        return None
+
+    def gpu_result_set0(self):
+        return None
+
+
+def make_workload(name, device, rank, world):
+    if name == "config1":
+        return SingleDecode(device, rank, 30, 29, uniform=True)
+    if name == "config2":
+        return SingleDecode(device, rank, 4096, 4095)
+    if name == "config3":
+        return RaggedBatch(device, rank)
+    if name == "config4":
+        return LongContext(device, rank, world)
+    raise SystemExit(f"unknown workload {name}")
+
+
+# ---------------------------------------------------------------------------
+def timed_graph_run(torch, wl, steps, warmup, stream, dist_on):
+    """Capture one replay of every buffer set (and a remainder) as CUDA graphs; time K steps."""
+    with torch.cuda.stream(stream):
+        for i in range(max(warmup, 1)):
+            wl.launch(i)
+    torch.cuda.synchronize()
+    graphs = {}
+    use_graphs = not (dist_on and wl.launches_per_step > 1)
+
+    def graph_of(n):
+        if n not in graphs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(n):
+                    wl.launch(i)
+            graphs[n] = g
+        return graphs[n]
+
+    n = wl.sets
+    if use_graphs:
+        graph_of(n)
+        if steps % n:
+            graph_of(steps % n)
+        with torch.cuda.stream(stream):
+            graphs[n].replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        if use_graphs:
+            for _ in range(steps // n):
+                graphs[n].replay()
+            if steps % n:
+                graphs[steps % n].replay()
+        else:
+            for i in range(steps):
+                wl.launch(i)
+        end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.monotonic()
+    if dist_on:
+        torch.distributed.barrier()
+    graphs.clear()
+    return start.elapsed_time(end), (t0, t1)
+
+
+def e2e_run(torch, wl, steps, device):
+    host = wl.e2e_inputs()
+    wl.e2e_step(host)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        out = wl.e2e_step(host)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    h2d = sum(x.numel() * x.element_size() for x in host)
+    d2h = out.numel() * out.element_size()
+    return dt, h2d, d2h
+
+
+def cpu_baseline(wl, budget_s=10.0):
+    """Thread-parallel float64 restatement of the golden on this host (kind "port")."""
+    import numpy as np
+    from oracle import check_rows
+    from oracle.parallel import gqa_golden_parallel
+    inp = wl.oracle_inputs()
+    if inp is None:
+        # ragged / sharded workloads: time the restatement on a config-2-sized sample
+        import torch
+        g = torch.Generator().manual_seed(1)
+        S = 4096
+
+        def bits(t):
+            return t.to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint16)
+        inp = (bits(torch.randn(32, 128, generator=g)), bits(torch.randn(8, S, 128, generator=g)),
+               bits(torch.randn(8, S, 128, generator=g)), S, S - 1)
+        gpu = None
+    else:
+        gpu = wl.gpu_result_set0()
+    q, k, v, s, qpos = inp
+    threads = os.cpu_count() or 1
+    from concurrent.futures import ThreadPoolExecutor
+    pool = ThreadPoolExecutor(max_workers=threads)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        ref = gqa_golden_parallel(q, k, v, s, qpos, pool=pool)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= budget_s or reps >= 200:
+            break
+    pool.shutdown()
+    out = {"value": round(kv_bytes(qpos + 1) * reps / dt / 1e9, 4), "unit": UNIT, "cores": threads,
+           "kind": "port",
+           "sample": f"{reps} x SEQ_LEN={s} decode(s) by the numpy float64 restatement (oracle/parallel.py), "
+                     f"{dt:.1f} s on {threads} threads"}
+    if gpu is not None:
+        res = check_rows(ref, gpu, 64)
+        out["gpu_vs_port_ulp"] = {"max": res.worst_ulp, "mean": round(res.mean_ulp, 5), "pass_64": res.passed}
+    return out
+
+
+def reference_arm(args, rank, world):
+    """`--impl reference`: the reference algorithm on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle.parallel import gqa_golden_parallel
+    cfg = {"config1": (30, 29), "config2": (4096, 4095), "config3": (4352, 4351), "config4": (131072, 131071)}
+    s, qpos = cfg[args.workload]
+    g = torch.Generator().manual_seed(20260805)
+
+    def bits(t):
+        return t.to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint16)
+    threads = os.cpu_count() or 1
+    pool = ThreadPoolExecutor(max_workers=threads)
+    q = bits(torch.randn(32, 128, generator=g))
+    probe_n = min(s, 4096)
+    kp, vp = bits(torch.randn(8, probe_n, 128, generator=g)), bits(torch.randn(8, probe_n, 128, generator=g))
+    t = time.perf_counter()
+    gqa_golden_parallel(q, kp, vp, probe_n, probe_n - 1, pool=pool)
+    t_probe = time.perf_counter() - t
+    per_key = t_probe / probe_n
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    n = int(max(64, min(s, budget / per_key)))
+    k, v = bits(torch.randn(8, n, 128, generator=g)), bits(torch.randn(8, n, 128, generator=g))
+    for _ in range(args.warmup):
+        gqa_golden_parallel(q, k, v, n, n - 1, pool=pool)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        gqa_golden_parallel(q, k, v, n, n - 1, pool=pool)
+    dt = time.perf_counter() - t0
+    pool.shutdown()
+    value = kv_bytes(n) * args.steps / dt / 1e9
+    sample = (f"each step: the first {n} keys of the SEQ_LEN={s} workload (float64 numpy restatement of "
+              f"gen_gqa_wrapper_vectors.py:121-139, {threads} threads)")
+    print(json.dumps({
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic N(0,1) seeded",
+        "impl": "reference", "config": {"workload": args.workload, "seq_len": s, "sample_keys": n},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=("config1", "config2", "config3", "config4"), default="config2")
+    ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank, world)
+        return
+
+    import torch
+    from attention_accelerator_b200.build import build_library
+    if rank == 0 or world == 1:
+        build_library()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist_on = world > 1
+    if dist_on:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+        build_library()
+    wl = make_workload(args.workload, device, rank, world)
+    stream = torch.cuda.Stream(device)
+    sampler = ClockSampler(local) if rank == 0 else None
+    ms, window = timed_graph_run(torch, wl, args.steps, args.warmup, stream, dist_on)
+    if sampler:
+        sampler.mark(*window)
+    if dist_on:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    scale = world if wl.scaling == "weak" else 1
+    value = wl.bytes_per_step * scale / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = peak_hbm()
+    per_gpu_bytes = wl.bytes_per_step if wl.scaling == "weak" else wl.bytes_per_step / world
+    achieved = per_gpu_bytes / (ms_step * 1e-3) / 1e9
+
+    e2e_dt, h2d, d2h = e2e_run(torch, wl, args.e2e_steps, device)
+    if dist_on:
+        t = torch.tensor([e2e_dt], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_dt = float(t.item())
+    e2e_value = wl.bytes_per_step * scale * args.e2e_steps / e2e_dt / 1e9
+    clocks = sampler.stop() if sampler else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(wl, args.cpu_budget)
+
+    traffic = None
+    tpath = ROOT / "profiles" / f"traffic_{wl.name}.json"
+    if tpath.is_file():
+        traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True,
+            "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic, seeded torch RNG (N(0,1) unless the workload says otherwise)",
+            "config": dict(wl.config(), parallelism=(f"dp{world} (independent sequences per GPU)"
+                                                     if wl.scaling == "weak" else wl.config().get("parallelism"))),
+            "pct_of_peak_hbm": round(100 * achieved / peak, 2),
+            "query_heads_per_s": round(wl.qheads_per_step * scale / (ms_step * 1e-3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "algorithmic_bytes_per_launch": per_gpu_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": args.e2e_steps},
+            "gpu_launches": args.steps * wl.launches_per_step,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

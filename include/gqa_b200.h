@@ -1,0 +1,206 @@
+/*
+ * gqa_b200.h -- C ABI of the B200 (sm_100a) GQA decode-attention library.
+ *
+ * The library computes, for one decode token per sequence, the grouped-query
+ * attention the reference accelerator implements: RoPE (theta 500000,
+ * rotate_half pairing) on Q at QUERY_POSITION and on every K row at its own
+ * position, Q.K scaled by `scale`, the hardware mask
+ *     key_valid(p) = (p < SEQ_LEN) && (p <= QUERY_POSITION),
+ * online softmax, weighted-V accumulation and reciprocal normalisation, for 32
+ * Q heads over 8 KV heads (group 4, head_dim 128), producing BF16 [32][128]
+ * output rows.
+ *
+ * Everything here is plain C: pointers, sizes and a `void*` CUDA stream handle
+ * (a cudaStream_t; NULL is the legacy default stream).  BF16 tensors are passed
+ * as `const void*` to 2-byte BF16 codes.  All device pointers must be 16-byte
+ * aligned and every stride (in elements) a multiple of 8.  Calls are
+ * asynchronous on `stream` and re-entrant across streams as long as each
+ * concurrent call has its own workspace.
+ *
+ * Status codes: every entry point returns GQA_OK (0) or a positive GQA_ERR_*
+ * code.  Configuration errors are detected on the host before anything is
+ * launched, mirroring the reference's start-time `config_error`
+ * (gqa_attention_wrapper.v:230-237) and the generator's argument checks
+ * (pyfiles/gen_gqa_wrapper_vectors.py:57-78).
+ */
+#ifndef GQA_B200_H
+#define GQA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum gqa_status {
+    GQA_OK = 0,
+    GQA_ERR_GEOMETRY = 1,          /* N_Q_HEADS/N_KV_HEADS/HEAD_DIM/TILE_DIM != 32/8/128/16 */
+    GQA_ERR_SEQ_LEN = 2,           /* SEQ_LEN == 0 */
+    GQA_ERR_N_KV_TILES = 3,        /* N_KV_TILES != ceil(SEQ_LEN / KV_BLOCK_LEN) */
+    GQA_ERR_SCALE = 4,             /* SCALE_FACTOR == 0 (or not finite) */
+    GQA_ERR_QUERY_POSITION = 5,    /* QUERY_POSITION >= SEQ_LEN */
+    GQA_ERR_KV_BLOCK_LEN = 6,      /* KV_BLOCK_LEN == 0 */
+    GQA_ERR_GROUP_SIZE = 7,        /* GROUP_SIZE != N_Q_HEADS / N_KV_HEADS */
+    GQA_ERR_NULL_POINTER = 8,
+    GQA_ERR_ALIGNMENT = 9,         /* pointer not 16-byte aligned or stride not a multiple of 8 */
+    GQA_ERR_WORKSPACE = 10,        /* workspace missing or smaller than gqa_workspace_bytes() */
+    GQA_ERR_BATCH = 11,            /* batch < 1, or a per-sequence descriptor is invalid */
+    GQA_ERR_KV_RANGE = 12,         /* stored key range [pos_begin, pos_end) invalid */
+    GQA_ERR_CUDA = 13,             /* a CUDA runtime call (launch, attribute, copy) failed */
+    GQA_ERR_DEVICE_TIMEOUT = 14,   /* a bounded wait inside a kernel gave up (see gqa_read_status) */
+    GQA_ERR_UNSUPPORTED_DEVICE = 15, /* current device is not sm_100 */
+    GQA_ERR_ROPE_THETA = 16        /* rope_theta <= 0 or not finite */
+};
+
+/* GQA_FLAG_* values for gqa_params.flags. */
+#define GQA_FLAG_PARTIAL_OUT 0x1u  /* write FP32 partials (see gqa_partial_row) instead of BF16 rows */
+
+/*
+ * Call parameters.  The first block mirrors the reference's AXI-Lite register
+ * map (axi_lite_regs.v:5-24) and RTL parameters (gqa_attention_wrapper.v:47-68);
+ * the rest describes where the tensors live.  Strides are in elements.
+ *
+ *   Q   : q  + b*q_batch_stride + qh*q_head_stride + d
+ *   K/V : k  + row*k_pos_stride + kh*k_head_stride + d,  row = kv_start + (p - pos_begin)
+ *   out : out + b*out_batch_stride + qh*out_head_stride + d
+ *
+ * Head-major transport order ([8][KV_INPUT_LEN][128], gen_gqa_wrapper_vectors.py:116-119)
+ * is k_pos_stride=128, k_head_stride=KV_INPUT_LEN*128; a position-major KV cache
+ * ([S][8][128]) is k_pos_stride=1024, k_head_stride=128.
+ */
+typedef struct gqa_params {
+    uint32_t n_q_heads;       /* 0x08 N_Q_HEADS      (must be 32)  */
+    uint32_t n_kv_heads;      /* 0x0C N_KV_HEADS     (must be 8)   */
+    uint32_t head_dim;        /* 0x10 HEAD_DIM       (must be 128) */
+    uint32_t tile_dim;        /* 0x14 TILE_DIM       (must be 16; the AXIS beat width, no effect on layout) */
+    uint32_t seq_len;         /* 0x18 SEQ_LEN        (single-sequence calls) */
+    uint32_t n_kv_tiles;      /* 0x1C N_KV_TILES     (single-sequence calls) */
+    float    scale;           /* 0x24 SCALE_FACTOR, as a float: the golden uses exactly 1/sqrt(128) */
+    uint32_t query_position;  /* 0x28 QUERY_POSITION (single-sequence calls) */
+    uint32_t kv_block_len;    /* KV_BLOCK_LEN: keys per hardware block (padding granularity) */
+    uint32_t group_size;      /* GROUP_SIZE contract: N_Q_HEADS / N_KV_HEADS */
+    float    rope_theta;      /* 500000 for Llama-3 */
+    uint32_t flags;           /* GQA_FLAG_* */
+    int64_t  q_batch_stride, q_head_stride;
+    int64_t  k_pos_stride, k_head_stride;
+    int64_t  v_pos_stride, v_head_stride;
+    int64_t  out_batch_stride, out_head_stride;
+    uint8_t *mask_out;        /* optional debug export: key_valid() per padded key position */
+    int64_t  mask_stride;     /* bytes between sequences in mask_out */
+} gqa_params;
+
+/*
+ * One sequence of a batched call.  The keys this call reads are the absolute
+ * positions [pos_begin, pos_end) intersected with the visible set
+ * [0, min(seq_len, query_position + 1)); key p is stored at row
+ * kv_start + (p - pos_begin).  pos_begin=0, pos_end=seq_len is a whole
+ * sequence; a sequence shard on one GPU of several uses its own sub-range.
+ */
+typedef struct gqa_seq_desc {
+    int64_t kv_start;
+    int32_t seq_len;
+    int32_t query_position;
+    int32_t pos_begin;
+    int32_t pos_end;
+} gqa_seq_desc;
+
+/* FP32 partial result for one Q head, written with GQA_FLAG_PARTIAL_OUT:
+ * acc = sum_p 2^(s_p - m) * V_p, l = sum_p 2^(s_p - m), s_p the score in log2
+ * units.  A head with no keys has m = -inf, l = 0, acc = 0.  out_head_stride and
+ * out_batch_stride are then in floats and must be >= 132 / >= 32*132. */
+typedef struct gqa_partial_row {
+    float acc[128];
+    float m;
+    float l;
+    float pad[2];
+} gqa_partial_row;
+
+/* Message for a status code (static string). */
+const char *gqa_status_string(int status);
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int gqa_version(void);
+
+/* 1 if `device` is an sm_100 GPU this library was compiled for, else 0. */
+int gqa_device_supported(int device);
+
+/*
+ * Host-side configuration check of a single-sequence call, without touching the
+ * GPU.  Replaces the START-time config_error (gqa_attention_wrapper.v:230-237)
+ * and the generator's checks (gen_gqa_wrapper_vectors.py:57-78).
+ */
+int gqa_validate(const gqa_params *p);
+
+/*
+ * Bytes of device workspace a call needs (0 on invalid input).  `descs` is the
+ * host copy of the batch's descriptors, or NULL with batch == 1 for a
+ * single-sequence call described by p->seq_len / p->query_position.
+ * The workspace must be zero-filled once when it is allocated; every call
+ * leaves it zeroed again (its split counters reset themselves).
+ */
+size_t gqa_workspace_bytes(const gqa_params *p, const gqa_seq_desc *descs, int batch);
+
+/*
+ * Single-token decode of one sequence: the operation the reference performs
+ * between START (axi_lite_regs.v:147-151) and the last output row
+ * (gqa_attention_wrapper.v:186-222); numerically the golden of
+ * pyfiles/gen_gqa_wrapper_vectors.py:121-139.
+ * q: [32][128] BF16; k, v: the key/value rows (layout from the strides);
+ * out: [32][128] BF16 (or gqa_partial_row[32] with GQA_FLAG_PARTIAL_OUT).
+ */
+int gqa_decode(const void *q, const void *k, const void *v, void *out,
+               const gqa_params *p, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Batched (ragged) decode: one query token per sequence, B sequences.  The
+ * per-sequence register values come from `descs`; `host_descs` is the same
+ * array in host memory (used to validate and plan), `dev_descs` in device
+ * memory (read by the kernel).  p->seq_len / n_kv_tiles / query_position are
+ * ignored.  The reference handles one sequence per START (gqa_controller.v:140-277);
+ * this entry point runs B of them in one launch.
+ */
+int gqa_decode_batched(const void *q, const void *k, const void *v, void *out,
+                       const gqa_params *p, const gqa_seq_desc *host_descs,
+                       const gqa_seq_desc *dev_descs, int batch,
+                       void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Log-sum-exp combine of `n_parts` FP32 partial results (gqa_partial_row) into
+ * BF16 rows: out = sum_s 2^(m_s-M) acc_s / sum_s 2^(m_s-M) l_s with M = max_s m_s.
+ * This is the rescale-and-normalise of flash_softmax.v:233-512 and
+ * output_accumulator.v:398-687 applied across sequence shards.
+ * partials: part s, sequence b, head h at partials + s*part_stride + b*batch_stride + h*132 floats.
+ */
+int gqa_combine_partials(const float *partials, int n_parts, int64_t part_stride,
+                         int64_t batch_stride, int batch, void *out,
+                         int64_t out_batch_stride, int64_t out_head_stride, void *stream);
+
+/*
+ * RoPE of `rows` 128-element BF16 rows, row r at positions[r], to FP32 rows:
+ * the rotation of rope_unit.v / rope_half_split (gen_gqa_wrapper_vectors.py:25-35)
+ * with the same device code the decode kernel uses.
+ */
+int gqa_rope_rows(const void *x, const int32_t *positions, float *out, int rows,
+                  float rope_theta, void *stream);
+
+/*
+ * The RoPE ROM tables of tools/gen_rope_rom.py:41-57, computed on the host:
+ * phase[i] = round(theta^(-i/(head_dim/2)) * 2^32 / 2pi) mod 2^32 (head_dim/2 entries);
+ * sincos[a] = (bf16(cos 2pi a/N) << 16) | bf16(sin 2pi a/N), N = 2^addr_bits.
+ */
+int gqa_rope_phase_rom(uint32_t *phase, int head_dim, double rope_theta);
+int gqa_rope_sincos_rom(uint32_t *sincos, int addr_bits);
+
+/*
+ * Read (and clear) the device status word a kernel leaves in `workspace`:
+ * GQA_OK, or GQA_ERR_DEVICE_TIMEOUT if a bounded wait gave up.  Synchronises
+ * `stream`.  Plays the part of ERROR_FLAGS/STATUS (axi_lite_regs.v:153-157,178).
+ */
+int gqa_read_status(void *workspace, void *stream, int *device_status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GQA_B200_H */

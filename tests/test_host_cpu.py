@@ -1,0 +1,154 @@
+"""Host-side logic of the C ABI and the Python API; runs without a GPU.
+
+* the library loads and exports every function ``include/gqa_b200.h`` declares;
+* ``gqa_validate`` rejects exactly what the RTL's ``config_error``
+  (gqa_attention_wrapper.v:230-237) and the generator (gen_gqa_wrapper_vectors.py:57-78) reject;
+* the ROM tables computed by the library are byte-identical to ``tools/gen_rope_rom.py``;
+* the ``.mem`` codec matches the oracle's restatement of gqa_reference.py;
+* the product package never imports the oracle and has no fallback when the library is absent.
+"""
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import attention_accelerator_b200 as gqa
+from attention_accelerator_b200 import _lib, memfile
+from attention_accelerator_b200.api import make_params
+from conftest import GOLDEN, ROOT
+from oracle.bf16 import mem_text, read_mem_array
+
+HEADER = ROOT / "include" / "gqa_b200.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gqa_\w+)\s*\(", text)))
+
+
+def test_header_declarations_match_binding():
+    assert declared_functions() == _lib.exported_symbols()
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    nm = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True)
+    exported = set(re.findall(r"\bT (gqa_\w+)", nm.stdout))
+    assert set(declared_functions()) <= exported
+
+
+def test_struct_layouts():
+    assert ctypes.sizeof(_lib.GqaSeqDesc) == 24
+    assert ctypes.sizeof(_lib.GqaParams) == 12 * 4 + 8 * 8 + 8 + 8
+
+
+def _validate(**kw) -> int:
+    p = make_params(**kw)
+    return _lib.load().gqa_validate(ctypes.byref(p))
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(seq_len=30), _lib.GQA_OK),
+    (dict(seq_len=30, n_q_heads=31), _lib.GQA_ERR_GEOMETRY),      # tb_gqa_attention_wrapper.sv:323
+    (dict(seq_len=30, n_kv_heads=7), _lib.GQA_ERR_GEOMETRY),
+    (dict(seq_len=30, head_dim=64), _lib.GQA_ERR_GEOMETRY),
+    (dict(seq_len=30, tile_dim=8), _lib.GQA_ERR_GEOMETRY),
+    (dict(seq_len=0, n_kv_tiles=0), _lib.GQA_ERR_SEQ_LEN),
+    (dict(seq_len=30, n_kv_tiles=3), _lib.GQA_ERR_N_KV_TILES),
+    (dict(seq_len=30, n_kv_tiles=1), _lib.GQA_ERR_N_KV_TILES),
+    (dict(seq_len=32, n_kv_tiles=2), _lib.GQA_OK),
+    (dict(seq_len=33, n_kv_tiles=2), _lib.GQA_ERR_N_KV_TILES),
+    (dict(seq_len=17, kv_block_len=4, n_kv_tiles=5), _lib.GQA_OK),
+    (dict(seq_len=30, scale=0.0), _lib.GQA_ERR_SCALE),
+    (dict(seq_len=30, scale=float("nan")), _lib.GQA_ERR_SCALE),
+    (dict(seq_len=30, query_position=30), _lib.GQA_ERR_QUERY_POSITION),
+    (dict(seq_len=30, query_position=0), _lib.GQA_OK),
+    (dict(seq_len=30, kv_block_len=0, n_kv_tiles=0), _lib.GQA_ERR_KV_BLOCK_LEN),
+    (dict(seq_len=30, group_size=2), _lib.GQA_ERR_GROUP_SIZE),
+    (dict(seq_len=30, rope_theta=0.0), _lib.GQA_ERR_ROPE_THETA),
+    (dict(seq_len=131072), _lib.GQA_OK),
+])
+def test_validate_mirrors_config_error(kw, status):
+    assert _validate(**kw) == status
+
+
+def test_api_raises_config_error_without_gpu():
+    with pytest.raises(gqa.GqaConfigError):
+        gqa.validate(seq_len=30, n_q_heads=31)
+    import torch
+    q = torch.zeros((32, 128), dtype=torch.bfloat16)
+    k = torch.zeros((30, 8, 128), dtype=torch.bfloat16)
+    with pytest.raises(gqa.GqaConfigError):
+        gqa.decode(q, k, k, seq_len=30, query_position=30)
+
+
+def test_decode_rejects_bad_pointers_before_launch():
+    lib = _lib.load()
+    p = make_params(seq_len=30)
+    assert lib.gqa_decode(None, None, None, None, ctypes.byref(p), None, 0, None) == _lib.GQA_ERR_NULL_POINTER
+    p.q_head_stride = 128
+    p.k_pos_stride = p.v_pos_stride = 1024
+    p.k_head_stride = p.v_head_stride = 128
+    assert lib.gqa_decode(8, 16, 16, 16, ctypes.byref(p), None, 0, None) == _lib.GQA_ERR_ALIGNMENT
+    p.k_pos_stride = 1001
+    assert lib.gqa_decode(16, 16, 16, 16, ctypes.byref(p), None, 0, None) == _lib.GQA_ERR_ALIGNMENT
+
+
+@pytest.mark.parametrize("bits", [10, 14])
+def test_library_rom_tables_match_reference(bits, manifest):
+    phase = gqa.rope_phase_rom()
+    sincos = gqa.rope_sincos_rom(bits)
+    phase_text = "".join(f"{p:08x}\n" for p in phase)
+    sincos_text = "".join(f"{s:08x}\n" for s in sincos)
+    want = manifest["rope_rom"][f"tools_bits{bits}"]
+    assert hashlib.sha256(phase_text.encode()).hexdigest() == want["rope_phase_rom.mem"]
+    assert hashlib.sha256(sincos_text.encode()).hexdigest() == want["rope_sincos_rom.mem"]
+
+
+def test_mem_codec_matches_oracle():
+    rng = np.random.default_rng(0)
+    rows = rng.integers(0, 1 << 16, size=(37, 16), dtype=np.uint16)
+    text = memfile.format_mem_text(rows)
+    assert text == mem_text(rows.tolist())
+    np.testing.assert_array_equal(memfile.parse_mem_text(text, 16), rows)
+    golden_path = GOLDEN / "cases" / "random_len30" / "gqa_golden.mem"
+    np.testing.assert_array_equal(memfile.read_mem(golden_path, 128), read_mem_array(golden_path, 128))
+
+
+def test_mem_compare_rule():
+    g = np.full((1, 128), 0x3F80, dtype=np.uint16)
+    a = g.copy()
+    a[0, 0] += 64
+    assert memfile.compare_rows(g, a, 64)["failures"] == 0
+    a[0, 0] += 1
+    assert memfile.compare_rows(g, a, 64)["failures"] == 1
+
+
+def test_product_never_imports_the_oracle():
+    pkg = ROOT / "attention_accelerator_b200"
+    for path in list(pkg.rglob("*.py")) + [pkg / "bin" / "vivado"]:
+        text = path.read_text()
+        assert not re.search(r"^\s*(from|import)\s+oracle\b", text, re.M), path
+
+
+def test_no_fallback_when_library_missing(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "LIB_PATH", tmp_path / "missing.so")
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(RuntimeError, match="missing"):
+        _lib.load()
+
+
+def test_plan_batch_descriptors_on_host():
+    plan = gqa.plan_batch([5, 9, 1], query_positions=[4, 3, 0], device=__import__("torch").device("cpu"))
+    assert [d.kv_start for d in plan.host] == [0, 5, 14]
+    assert [d.pos_end for d in plan.host] == [5, 9, 1]
+    assert plan.device.numel() == 3 * 24

@@ -1,0 +1,125 @@
+"""The oracle pinned against files the reference's own scripts wrote (sha256 + golden rows).
+
+If these pass, every regenerated input, config text, golden output, RoPE
+known-answer row and ROM table used by the GPU tests is byte-identical to what
+``pyfiles/gen_gqa_wrapper_vectors.py``, ``pyfiles/gen_rope_test_vectors.py`` and
+``tools/gen_rope_rom.py`` produce (tests/golden/make_golden.py recorded them).
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, case_kwargs
+from oracle import check_rows, generate_case, gqa_golden
+from oracle.bf16 import bf16_to_f32, f32_to_bf16, read_mem_array, ulp_distance, unpack_bf16, pack_bf16
+from oracle.rope_rom import rom_texts
+from oracle.vectors import beats_text, rope_kat
+
+
+def sha(text: str) -> str:
+    return hashlib.sha256(text.encode()).hexdigest()
+
+
+def test_every_case_regenerates_byte_identical(manifest):
+    for name, entry in manifest["cases"].items():
+        case = generate_case(**case_kwargs(entry["args"]))
+        want = entry["sha256"]
+        assert sha(case.q_mem_text()) == want["gqa_q.mem"], name
+        assert sha(case.kv_mem_text("k")) == want["gqa_k.mem"], name
+        assert sha(case.kv_mem_text("v")) == want["gqa_v.mem"], name
+        assert sha(case.config_text()) == want["gqa_config.txt"], name
+        golden_file = GOLDEN / "cases" / name / "gqa_golden.mem"
+        assert hashlib.sha256(golden_file.read_bytes()).hexdigest() == want["gqa_golden.mem"], name
+
+
+@pytest.mark.parametrize("name", ["smoke_len1", "random_len15", "random_len17_bp", "random_len30",
+                                  "causal_len30_q7", "causal_len64_q0", "block8_len30_q20", "random_len256"])
+def test_oracle_golden_is_bit_identical(name, manifest):
+    case = generate_case(**case_kwargs(manifest["cases"][name]["args"]))
+    assert sha(case.golden_mem_text()) == manifest["cases"][name]["sha256"]["gqa_golden.mem"]
+
+
+def test_fast_oracle_agrees_with_exact(manifest):
+    for name in ("random_len256", "causal_len100_q63", "random_len1024"):
+        case = generate_case(**case_kwargs(manifest["cases"][name]["args"]))
+        golden = read_mem_array(GOLDEN / "cases" / name / "gqa_golden.mem", 128)
+        fast = case.golden_bits(exact=False)
+        assert check_rows(golden, fast, 0).worst_ulp <= 1
+
+
+def test_corpus_65536_is_the_len30_case(manifest):
+    """README.md:121-138: 65,536 valid elements select SEQ_LEN=30 with two pad rows."""
+    c = manifest["cases"]
+    assert c["corpus_65536"]["sha256"] == c["random_len30"]["sha256"]
+    case = generate_case(**case_kwargs(c["corpus_65536"]["args"]))
+    assert case.seq_len == 30 and case.kv_input_len == 32
+    assert "VALID_INPUT_BF16_VECTORS=65536" in case.config_text()
+    assert "TRANSPORT_BF16_VECTORS=69632" in case.config_text()
+
+
+def test_rope_known_answer_set(manifest):
+    x, golden = rope_kat()
+    assert sha(beats_text(x)) == manifest["rope_kat"]["sha256"]["in.mem"]
+    assert sha(beats_text(golden)) == manifest["rope_kat"]["sha256"]["golden.mem"]
+
+
+@pytest.mark.parametrize("bits", [10, 14])
+def test_rope_rom_tables(bits, manifest):
+    texts = rom_texts(addr_bits=bits)
+    want = manifest["rope_rom"][f"tools_bits{bits}"]
+    for fname, text in texts.items():
+        assert sha(text) == want[fname]
+    if bits == 14:
+        assert {f: sha(t) for f, t in texts.items()} == manifest["rope_rom"]["pyfiles_bits14"]
+
+
+def test_bf16_rounding_edges():
+    vals = np.array([0.0, -0.0, 1.0, 1.0 + 2**-8, 1.0 + 3 * 2**-8, 1e-40, -3.0e38, np.inf, -np.inf])
+    bits = f32_to_bf16(vals)
+    assert bits[3] == 0x3F80  # tie to even
+    assert bits[4] == 0x3F82
+    assert bits[7] == 0x7F80 and bits[8] == 0xFF80
+    np.testing.assert_array_equal(f32_to_bf16(bf16_to_f32(bits)), bits)
+
+
+def test_ulp_and_checker_rule():
+    assert ulp_distance(0x3F80, 0x3F81) == 1
+    assert ulp_distance(0x0001, 0x8001) == 2
+    golden = np.full((2, 128), 0x3F80, dtype=np.uint16)
+    actual = golden.copy()
+    actual[0, 5] = 0x3F80 + 65
+    res = check_rows(golden, actual, 64)
+    assert not res.passed and res.failures == 1 and res.worst_ulp == 65
+    # exponent fields <= 0x3d on both sides are exempt (check_gqa_output.py:61-64)
+    tiny_g = np.full((1, 128), 0x1E00, dtype=np.uint16)
+    tiny_a = np.full((1, 128), 0x1E90, dtype=np.uint16)
+    assert check_rows(tiny_g, tiny_a, 64).passed
+
+
+def test_mem_line_order():
+    line = pack_bf16(list(range(16)))
+    assert line.endswith("0000") and line.startswith("000f")
+    assert unpack_bf16(line, 16) == list(range(16))
+
+
+def test_golden_causal_only_reads_visible_keys():
+    """Changing keys after QUERY_POSITION changes nothing (the implicit mask of :132-133)."""
+    case = generate_case(40, mode="random", seed=5, query_position=9)
+    base = case.golden_bits()
+    case.k_bits[:, 10:] ^= 0x1234
+    case.v_bits[:, 10:] ^= 0x0F0F
+    np.testing.assert_array_equal(case.golden_bits(), base)
+
+
+def test_generator_argument_checks():
+    with pytest.raises(ValueError):
+        generate_case(0)
+    with pytest.raises(ValueError):
+        generate_case(10, query_position=10)
+    with pytest.raises(ValueError):
+        generate_case(target_input_vectors=65537)
+    with pytest.raises(ValueError):
+        generate_case(10, kv_block_len=0)
