@@ -5,6 +5,9 @@
 #include "gqa_device.cuh"
 #include "gqa_internal.h"
 
+#include <cudaTypedefs.h>
+
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <mutex>
@@ -56,6 +59,49 @@ int current_device(int* sms) {
     return GQA_OK;
 }
 
+// cuTensorMapEncodeTiled from the driver, fetched once through the runtime (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 3-D tensor map over K or V: (head_dim, row, head) when rows are the smaller
+// stride (head-major), else (head_dim, head, row).  One box = one tile of
+// consecutive rows of one head; rows past `rows` read as zeros.
+int make_kv_map(CUtensorMap* map, const void* base, int64_t pos_stride, int64_t head_stride, int64_t rows,
+                int* rows_inner) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return GQA_ERR_CUDA;
+    const cuuint64_t tile = (cuuint64_t)gqa::decode_tile_keys();
+    cuuint64_t dims[3];
+    cuuint64_t strides[2];
+    cuuint32_t box[3];
+    const cuuint32_t estr[3] = {1, 1, 1};
+    if (pos_stride <= head_stride) {
+        dims[0] = gqa::kHeadDim; dims[1] = (cuuint64_t)rows; dims[2] = gqa::kNumKVHeads;
+        strides[0] = (cuuint64_t)pos_stride * 2; strides[1] = (cuuint64_t)head_stride * 2;
+        box[0] = gqa::kHeadDim; box[1] = (cuuint32_t)tile; box[2] = 1;
+        *rows_inner = 1;
+    } else {
+        dims[0] = gqa::kHeadDim; dims[1] = gqa::kNumKVHeads; dims[2] = (cuuint64_t)rows;
+        strides[0] = (cuuint64_t)head_stride * 2; strides[1] = (cuuint64_t)pos_stride * 2;
+        box[0] = gqa::kHeadDim; box[1] = 1; box[2] = (cuuint32_t)tile;
+        *rows_inner = 0;
+    }
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? GQA_OK : GQA_ERR_ALIGNMENT;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 bool stride_ok(int64_t s) { return s >= 0 && (s % 8) == 0; }
 
@@ -75,7 +121,7 @@ int check_layout(const void* q, const void* k, const void* v, const void* out, c
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return GQA_ERR_ALIGNMENT;
     if (!stride_ok(p->q_batch_stride) || !stride_ok(p->q_head_stride) || !stride_ok(p->k_head_stride) ||
         !stride_ok(p->v_head_stride) || !stride_ok(p->k_pos_stride) || !stride_ok(p->v_pos_stride) ||
-        p->k_pos_stride == 0 || p->v_pos_stride == 0)
+        p->k_pos_stride == 0 || p->v_pos_stride == 0 || p->k_head_stride == 0 || p->v_head_stride == 0)
         return GQA_ERR_ALIGNMENT;
     if (p->flags & GQA_FLAG_PARTIAL_OUT) {
         if (p->out_head_stride < gqa::kPartialFloats || p->out_head_stride % 4 || p->out_batch_stride < 0 ||
@@ -99,7 +145,8 @@ int check_desc(const gqa::SeqDesc& d, bool need_keys) {
 struct Plan {
     int chunk = 0;
     int total_splits = 0;
-    size_t off_counters = 0, off_partials = 0, ws_bytes = 0;
+    int64_t kv_rows = 1;  // tensor-map row extent: one past the last stored row any key uses
+    size_t off_seqinfo = 0, off_partials = 0, ws_bytes = 0;
 };
 
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -108,8 +155,13 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // wave count (1..16) that minimises waves x (chunk + per-CTA overhead).
 Plan make_plan(const gqa::SeqDesc* d, int batch, int sms) {
     const int slots = sms / gqa::kNumKVHeads > 0 ? sms / gqa::kNumKVHeads : 1;
-    int64_t total = 0;
-    for (int b = 0; b < batch; ++b) total += gqa::seq_key_count(d[b]);
+    int64_t total = 0, longest = 0;
+    for (int b = 0; b < batch; ++b) {
+        total += gqa::seq_key_count(d[b]);
+        longest = std::max<int64_t>(longest, gqa::seq_key_count(d[b]));
+    }
+    // The last split of a sequence stages every split's partial in shared memory.
+    const int64_t min_chunk = (longest + gqa::decode_max_splits() - 1) / gqa::decode_max_splits();
     auto splits_for = [&](int chunk) {
         int64_t s = 0;
         for (int b = 0; b < batch; ++b) s += gqa::seq_splits(d[b], chunk);
@@ -123,6 +175,7 @@ Plan make_plan(const gqa::SeqDesc* d, int batch, int sms) {
         int64_t chunk = (total + (int64_t)slots * w - 1) / ((int64_t)slots * w);
         const int floor_chunk = (batch == 1 || w == 1) ? kMinChunk : kMinChunkMultiWave;
         if (chunk < floor_chunk) chunk = floor_chunk;
+        if (chunk < min_chunk) chunk = min_chunk;
         const int c = round8(chunk);
         const int64_t ctas = splits_for(c) * gqa::kNumKVHeads;
         const int64_t waves = (ctas + sms - 1) / sms;
@@ -135,8 +188,11 @@ Plan make_plan(const gqa::SeqDesc* d, int batch, int sms) {
     Plan pl;
     pl.chunk = best_chunk > 0 ? best_chunk : kMinChunk;
     pl.total_splits = (int)splits_for(pl.chunk);
-    pl.off_counters = kWsHeaderBytes;
-    pl.off_partials = pl.off_counters + align256((size_t)batch * gqa::kNumKVHeads * sizeof(uint32_t));
+    pl.kv_rows = 1;
+    for (int b = 0; b < batch; ++b)
+        pl.kv_rows = std::max<int64_t>(pl.kv_rows, d[b].kv_start + gqa::seq_key_count(d[b]));
+    pl.off_seqinfo = kWsHeaderBytes;
+    pl.off_partials = pl.off_seqinfo + align256((size_t)batch * sizeof(int2));
     pl.ws_bytes = pl.off_partials + (size_t)pl.total_splits * gqa::kNumKVHeads * gqa::kGroup *
                                         gqa::kPartialFloats * sizeof(float);
     return pl;
@@ -164,9 +220,17 @@ gqa::SeqDesc single_desc(const gqa_params* p) {
     return d;
 }
 
-void fill_args(gqa::DecodeArgs& a, const void* q, const void* k, const void* v, void* out, const gqa_params* p,
-               void* ws, const Plan& pl, int batch) {
+int fill_args(gqa::DecodeArgs& a, const void* q, const void* k, const void* v, void* out, const gqa_params* p,
+              void* ws, const Plan& pl, int batch) {
     std::memset(&a, 0, sizeof(a));
+    if (pl.kv_rows > 0x7FFFFFFF) return GQA_ERR_KV_RANGE;
+    int inner_k = 0, inner_v = 0;
+    int st = make_kv_map(&a.kmap, k, p->k_pos_stride, p->k_head_stride, pl.kv_rows, &inner_k);
+    if (st != GQA_OK) return st;
+    st = make_kv_map(&a.vmap, v, p->v_pos_stride, p->v_head_stride, pl.kv_rows, &inner_v);
+    if (st != GQA_OK) return st;
+    if (inner_k != inner_v) return GQA_ERR_ALIGNMENT;  // K and V must share one layout
+    a.kv_rows_inner = inner_k;
     a.q = static_cast<const __nv_bfloat16*>(q);
     a.k = static_cast<const __nv_bfloat16*>(k);
     a.v = static_cast<const __nv_bfloat16*>(v);
@@ -185,12 +249,13 @@ void fill_args(gqa::DecodeArgs& a, const void* q, const void* k, const void* v, 
     a.flags = p->flags;
     uint8_t* w = static_cast<uint8_t*>(ws);
     a.ws_status = reinterpret_cast<uint32_t*>(w);
-    a.ws_counters = reinterpret_cast<uint32_t*>(w + pl.off_counters);
+    a.ws_seqinfo = reinterpret_cast<int2*>(w + pl.off_seqinfo);
     a.ws_partials = reinterpret_cast<float*>(w + pl.off_partials);
     a.mask_out = p->mask_out;
     a.mask_stride = p->mask_stride;
     a.kv_block_len = (int)p->kv_block_len;
     rope_steps((double)p->rope_theta, a.rope_step, a.rot_step, a.rot_tile, gqa::decode_tile_keys());
+    return GQA_OK;
 }
 
 }  // namespace
@@ -275,10 +340,12 @@ int gqa_decode(const void* q, const void* k, const void* v, void* out, const gqa
     const Plan pl = make_plan(&d, 1, sms);
     if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
     gqa::DecodeArgs a;
-    fill_args(a, q, k, v, out, p, workspace, pl, 1);
+    st = fill_args(a, q, k, v, out, p, workspace, pl, 1);
+    if (st != GQA_OK) return st;
     a.descs = nullptr;
     a.single = d;
-    if (gqa::launch_decode(a, pl.total_splits * gqa::kNumKVHeads, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    if (gqa::launch_decode(a, pl.total_splits * gqa::kNumKVHeads, pl.total_splits, static_cast<cudaStream_t>(stream)) !=
+        cudaSuccess)
         return GQA_ERR_CUDA;
     return GQA_OK;
 }
@@ -305,10 +372,12 @@ int gqa_decode_batched(const void* q, const void* k, const void* v, void* out, c
     const Plan pl = make_plan(d, batch, sms);
     if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
     gqa::DecodeArgs a;
-    fill_args(a, q, k, v, out, p, workspace, pl, batch);
+    st = fill_args(a, q, k, v, out, p, workspace, pl, batch);
+    if (st != GQA_OK) return st;
     a.descs = reinterpret_cast<const gqa::SeqDesc*>(dev_descs);
     a.single = d[0];
-    if (gqa::launch_decode(a, pl.total_splits * gqa::kNumKVHeads, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    if (gqa::launch_decode(a, pl.total_splits * gqa::kNumKVHeads, pl.total_splits, static_cast<cudaStream_t>(stream)) !=
+        cudaSuccess)
         return GQA_ERR_CUDA;
     return GQA_OK;
 }

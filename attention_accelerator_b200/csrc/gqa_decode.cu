@@ -1,29 +1,30 @@
-// gqa_decode.cu -- split-KV flash-decoding kernel for GQA (32 Q heads over 8 KV
-// heads, head_dim 128) on sm_100a, plus the cross-shard log-sum-exp combine and
-// a stand-alone RoPE kernel.
+// gqa_decode.cu -- split-KV flash-decoding kernels for GQA (32 Q heads over 8 KV
+// heads, head_dim 128) on sm_100a: the decode kernel, the split merge, the
+// cross-shard log-sum-exp combine and a stand-alone RoPE kernel.
 //
-// What one CTA computes: the attention of the 4 Q heads of one KV head h of one
-// sequence b over a contiguous range of that sequence's visible keys (a
-// "split").  This is the reference's per-KV-head group loop
+// decode_kernel: one CTA computes the attention of the 4 Q heads of one KV head
+// h of one sequence b over a contiguous range of that sequence's visible keys
+// (a "split").  This is the reference's per-KV-head group loop
 // (gqa_controller.v:140-277: Q group -> K position -> block) with the key loop
 // cut into splits so that every SM streams K/V rows at once.
-//
-// Pipeline (per CTA):
-//   warp 8      producer: bulk-copies 64-key K and V tiles (16 KB each) into a
+//   warp 8      producer: one thread issues a TMA tensor copy per 64-key K tile
+//               and V tile (16 KB each, one head, any K/V strides) into a
 //               4-stage shared-memory ring, one mbarrier per stage and direction.
 //   warps 0..7  consumers: warp c owns keys [8c, 8c+8) of every tile, four at a
 //               time: 8 lanes per key, each lane 8 rotate_half pairs (16 of the
 //               128 dims).  Per key: RoPE of K (rope_unit.v), the 4 Q.K dot
 //               products in FP32 (bf16_dot_product_mac.v + scale_unit.v), a
-//               3-level shuffle reduction, the hardware mask (score_tag_fifo /
-//               gqa_attention_wrapper.v:279), online softmax in log2 units
+//               3-level shuffle reduction, online softmax in log2 units
 //               (flash_softmax.v:233-490) and the P.V accumulation
 //               (output_accumulator.v:244-536) with each lane owning 4 dims.
+//               The P.V of tile t-1 is interleaved with the Q.K of tile t.
 //   epilogue    the 8 warps' (m, l, acc) merge through shared memory; a sequence
-//               with one split writes BF16 rows directly (O * 1/l,
-//               output_accumulator.v:546-687), otherwise each split publishes
-//               an FP32 partial to the workspace and the last split of (b, h)
-//               to arrive merges them.
+//               with one split writes its BF16 rows (O * 1/l,
+//               output_accumulator.v:546-687) directly, otherwise each split
+//               writes an FP32 partial to the workspace for split_merge_kernel.
+// Both kernels are launched with programmatic dependent launch: everything that
+// reads only the argument block (barrier set-up, RoPE tables) runs before
+// griddepcontrol.wait, overlapping the tail of the previous kernel in the stream.
 #include "gqa_device.cuh"
 #include "gqa_internal.h"
 
@@ -31,24 +32,49 @@ namespace gqa {
 
 namespace {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kTileKeys = 64;
+// 11 consumer warps + 1 producer warp = 12 warps: the most warps the 168
+// registers a consumer thread needs allow (64K registers per SM).
+constexpr int kConsumerWarps = 11;
+constexpr int kKeysPerWarp = 8;                             // keys of one tile per warp
+constexpr int kTileKeys = kConsumerWarps * kKeysPerWarp;    // 88 keys per pipeline tile
 constexpr int kStages = 4;
-constexpr int kKeysPerWarp = kTileKeys / kConsumerWarps;  // 8: two groups of 4
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kSteps = kKeysPerWarp / 4;                  // groups of 4 keys (8 lanes per key)
+static_assert(kSteps >= 1 && kSteps * 4 == kKeysPerWarp, "a warp takes whole groups of 4 keys");
 constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;  // + the producer warp
 constexpr int kTileBytes = kTileKeys * kRowBytes;
 constexpr int kStageBytes = 2 * kTileBytes;
 constexpr int kReanchorTiles = 32;  // exact RoPE phase every 32 tiles (2048 keys)
+// Epilogue: consumer thread tid owns outputs o = tid, tid + kConsumerThreads, ...
+// of the 4 x 128 (head, dim) outputs.
+constexpr int kOutputs = kGroup * kHeadDim;
 
+// Shared-memory layout.
 constexpr int kOffBars = kStages * kStageBytes;
 constexpr int kOffP = kOffBars + 2 * kStages * 8;
-constexpr int kOffAlpha = kOffP + kConsumerWarps * kKeysPerWarp * kGroup * 4;
-constexpr int kOffInfo = kOffAlpha + kConsumerWarps * kGroup * 4;
+constexpr int kPBytes = 2 * kConsumerWarps * kKeysPerWarp * kGroup * 8;  // [warp][2][key][head] (p, p)
+constexpr int kOffAlpha = kOffP + kPBytes;
+// RoPE tables shared by the CTA's lanes (float2 each, kPairs per row): Q
+// factors at QUERY_POSITION, the CTA's first-key factors, per-warp offsets
+// e^{i theta 8c}, per-slot offsets e^{i theta s}, and the 4-key and one-tile
+// advances.
+constexpr int kRopeQ = 0, kRopeBase = 1, kRopeWarp = 2, kRopeSlot = 2 + kConsumerWarps, kRopeStep = kRopeSlot + 4,
+              kRopeTile = kRopeStep + 1, kRopeRows = kRopeTile + 1;
+constexpr int kOffRope = kOffAlpha + 2 * kConsumerWarps * kGroup * 4;
+constexpr int kOffSteps = kOffRope + kRopeRows * kPairs * 8;  // u64 Q0.64 phase steps, copied from the arguments
+constexpr int kOffInfo = kOffSteps + kPairs * 8;
 constexpr int kSmemBytes = kOffInfo + 64;
-static_assert(kConsumerWarps * kGroup * kPartialFloats * 4 <= kOffBars, "combine buffer must fit the ring");
+static_assert(kConsumerWarps * kGroup * kPartialFloats * 4 <= kOffBars, "warp merge buffer fits the ring");
+
+// Splits per sequence that split_merge_kernel merges in one pass.
+constexpr int kMaxSplitsPerSeq = 64;
 
 __device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
+
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // Complex multiply of (re, im) pairs held as float2 lanes: (ar + i ai) * (br + i bi).
 __device__ __forceinline__ void cmul2(float2 ar, float2 ai, float2 br, float2 bi, float2& cr, float2& ci) {
@@ -57,32 +83,81 @@ __device__ __forceinline__ void cmul2(float2 ar, float2 ai, float2 br, float2 bi
     ci = __ffma2_rn(ar, bi, __fmul2_rn(ai, br));
 }
 
-// Exact RoPE factors of this lane's 8 pairs (8g .. 8g+7) at absolute position pos.
-__device__ __forceinline__ void rope_factors8(const DecodeArgs& a, int g, int64_t pos, float2 (&wr)[4],
-                                              float2 (&wi)[4]) {
+// Exact factors of this lane's 8 pairs (8g .. 8g+7) at absolute position pos,
+// from the shared copy of the phase steps.
+__device__ __forceinline__ void rope_exact8(const uint64_t* steps, int g, int64_t pos, float2 (&wr)[4],
+                                            float2 (&wi)[4]) {
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
-        const float2 f0 = rope_factor(a.rope_step[8 * g + 2 * jj], pos);
-        const float2 f1 = rope_factor(a.rope_step[8 * g + 2 * jj + 1], pos);
+        const float2 f0 = rope_factor(steps[8 * g + 2 * jj], pos);
+        const float2 f1 = rope_factor(steps[8 * g + 2 * jj + 1], pos);
         wr[jj] = make_float2(f0.x, f1.x);
         wi[jj] = make_float2(f0.y, f1.y);
     }
 }
 
-__device__ __forceinline__ void write_result(const DecodeArgs& a, int b, int qh, int dim, float acc, float m,
-                                             float l) {
-    if (a.flags & 1u) {
-        float* o = static_cast<float*>(a.out) + (int64_t)b * a.o_bstride + (int64_t)qh * a.o_hstride;
-        o[dim] = acc;
+// The 8 factors of pairs 8g..8g+7 from one row of the shared RoPE table.
+__device__ __forceinline__ void rope_row8(const float2* row, int g, float2 (&wr)[4], float2 (&wi)[4]) {
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+        const float4 f = *reinterpret_cast<const float4*>(row + 8 * g + 2 * jj);
+        wr[jj] = make_float2(f.x, f.z);
+        wi[jj] = make_float2(f.y, f.w);
+    }
+}
+
+// Copy the phase steps and the two fixed advances from the argument block to
+// shared memory: one load per thread, all in flight together.
+__device__ __forceinline__ void stage_rope_constants(const DecodeArgs& a, float2* rope, uint64_t* steps, int tid) {
+    if (tid < kPairs) {
+        steps[tid] = a.rope_step[tid];
+    } else if (tid < 2 * kPairs) {
+        rope[kRopeStep * kPairs + tid - kPairs] = a.rot_step[tid - kPairs];
+    } else if (tid < 3 * kPairs) {
+        rope[kRopeTile * kPairs + tid - 2 * kPairs] = a.rot_tile[tid - 2 * kPairs];
+    }
+}
+
+// Fill the exact rows of the shared RoPE table for a CTA whose Q sits at qpos
+// and whose first key is at first_pos (consumer threads, after the steps are staged).
+__device__ __forceinline__ void build_rope_table(const uint64_t* steps, float2* rope, int qpos, int64_t first_pos,
+                                                 int tid) {
+    constexpr int kExact = (2 + kConsumerWarps + 4) * kPairs;
+    constexpr int kIters = (kExact + kConsumerThreads - 1) / kConsumerThreads;
+#pragma unroll
+    for (int j = 0; j < kIters; ++j) {
+        const int f = tid + j * kConsumerThreads;
+        if (f < kExact) {
+            const int row = f / kPairs, i = f - row * kPairs;
+            const int64_t pos = row == kRopeQ      ? (int64_t)qpos
+                                : row == kRopeBase ? first_pos
+                                : row < kRopeSlot  ? (int64_t)(row - kRopeWarp) * kKeysPerWarp
+                                                   : (int64_t)(row - kRopeSlot);
+            rope[f] = rope_factor(steps[i], pos);
+        }
+    }
+}
+
+struct OutSpec {
+    void* out;
+    int64_t o_bstride, o_hstride;
+    uint32_t flags;
+};
+
+// One output element: BF16 acc/l (round to nearest even), or the FP32 partial row.
+__device__ __forceinline__ void write_result(const OutSpec& o, int b, int qh, int dim, float acc, float m, float l) {
+    if (o.flags & 1u) {
+        float* r = static_cast<float*>(o.out) + (int64_t)b * o.o_bstride + (int64_t)qh * o.o_hstride;
+        r[dim] = acc;
         if (dim == 0) {
-            o[128] = m;
-            o[129] = l;
-            o[130] = 0.f;
-            o[131] = 0.f;
+            r[128] = m;
+            r[129] = l;
+            r[130] = 0.f;
+            r[131] = 0.f;
         }
     } else {
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out) + (int64_t)b * a.o_bstride + (int64_t)qh * a.o_hstride;
-        o[dim] = __float2bfloat16_rn(acc / l);
+        __nv_bfloat16* r = static_cast<__nv_bfloat16*>(o.out) + (int64_t)b * o.o_bstride + (int64_t)qh * o.o_hstride;
+        r[dim] = __float2bfloat16_rn(acc / l);
     }
 }
 
@@ -90,19 +165,44 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
     uint64_t* empty = full + kStages;
-    float* pbuf = reinterpret_cast<float*>(smem + kOffP);
+    float2* pbuf = reinterpret_cast<float2*>(smem + kOffP);
     float* abuf = reinterpret_cast<float*>(smem + kOffAlpha);
+    float2* rope = reinterpret_cast<float2*>(smem + kOffRope);
+    uint64_t* steps = reinterpret_cast<uint64_t*>(smem + kOffSteps);
     int* info = reinterpret_cast<int*>(smem + kOffInfo);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const int tid = threadIdx.x;
     const int h = blockIdx.x % kNumKVHeads;
     const int gsplit = blockIdx.x / kNumKVHeads;
+    const bool single = a.descs == nullptr;
+
+    // ---- set-up that reads only the argument block: before the dependency wait
+    if (tid == kConsumerThreads) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        fence_barrier_init();
+        prefetch_tensormap(&a.kmap);
+        prefetch_tensormap(&a.vmap);
+    }
+    if (warp < kConsumerWarps) {
+        stage_rope_constants(a, rope, steps, tid);
+        named_barrier_sync(1, kConsumerThreads);
+        if (single) {
+            const int64_t first_pos = (int64_t)a.single.pos_begin + (int64_t)gsplit * a.chunk;
+            build_rope_table(steps, rope, a.single.query_position, first_pos, tid);
+        }
+    }
+    allow_dependent_launch();
+    grid_dependency_wait();
 
     // ---- which (sequence, split) this CTA owns: prefix sum of splits per sequence
     if (warp == 0) {
         int b = 0, split = gsplit;
-        if (a.descs != nullptr) {
+        if (!single) {
             int base = 0;
             b = -1;
             for (int b0 = 0; b0 < a.batch && b < 0; b0 += 32) {
@@ -130,18 +230,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             info[1] = split;
         }
     }
-    if (threadIdx.x == 32) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
-        fence_barrier_init();
-    }
     __syncthreads();
     const int b = info[0];
     const int split = info[1];
     if (b < 0) return;  // grid larger than the plan: nothing to do (uniform per CTA)
-    const SeqDesc d = a.descs != nullptr ? a.descs[b] : a.single;
+    const SeqDesc d = single ? a.single : a.descs[b];
     const int n_keys = seq_key_count(d);
     const int n_split = seq_splits(d, a.chunk);
     const int key0 = split * a.chunk;
@@ -150,44 +243,37 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const int64_t first_pos = (int64_t)d.pos_begin + key0;
     const int64_t first_row = d.kv_start + key0;
 
+    // The split merge finds each sequence's splits here.
+    if (split == 0 && h == 0 && tid == 0 && n_split > 1) a.ws_seqinfo[b] = make_int2(gsplit, n_split);
+
     // ======================= producer warp =======================
+    // One elected thread issues, per tile, one TMA box for K and one for V
+    // (64 rows of one head, whatever the K/V strides), then drains its copies.
     if (warp == kConsumerWarps) {
-        const __nv_bfloat16* kb = a.k + first_row * a.k_pstride + (int64_t)h * a.k_hstride;
-        const __nv_bfloat16* vb = a.v + first_row * a.v_pstride + (int64_t)h * a.v_hstride;
-        const bool k_rows_contig = a.k_pstride == kHeadDim;
-        const bool v_rows_contig = a.v_pstride == kHeadDim;
+        if (lane != 0) return;
         const uint64_t pol = l2_evict_first_policy();
         int issued = 0;
         bool ok = true;
         for (int t = 0; t < n_tiles; ++t) {
             const int st = t % kStages;
-            if (t >= kStages) ok = mbar_wait(&empty[st], ((t / kStages) - 1) & 1);
-            if (!__all_sync(0xffffffffu, ok)) {
+            if (t >= kStages && !mbar_wait(&empty[st], ((t / kStages) - 1) & 1)) {
                 ok = false;
                 break;
             }
-            const int rows = min(kTileKeys, cnt - t * kTileKeys);
             uint8_t* kd = smem + st * kStageBytes;
             uint8_t* vd = kd + kTileBytes;
-            if (lane == 0) mbar_arrive_expect_tx(&full[st], rows * 2 * kRowBytes);
-            __syncwarp();
-            const __nv_bfloat16* ks = kb + (int64_t)t * kTileKeys * a.k_pstride;
-            const __nv_bfloat16* vs = vb + (int64_t)t * kTileKeys * a.v_pstride;
-            if (k_rows_contig) {
-                if (lane == 0) bulk_load(kd, ks, rows * kRowBytes, &full[st], pol);
+            mbar_arrive_expect_tx(&full[st], 2 * kTileBytes);
+            const int row = static_cast<int>(first_row + (int64_t)t * kTileKeys);
+            if (a.kv_rows_inner) {
+                tma_load_3d(kd, &a.kmap, 0, row, h, &full[st], pol);
+                tma_load_3d(vd, &a.vmap, 0, row, h, &full[st], pol);
             } else {
-                for (int r = lane; r < rows; r += 32)
-                    bulk_load(kd + r * kRowBytes, ks + (int64_t)r * a.k_pstride, kRowBytes, &full[st], pol);
-            }
-            if (v_rows_contig) {
-                if (lane == 1) bulk_load(vd, vs, rows * kRowBytes, &full[st], pol);
-            } else {
-                for (int r = lane; r < rows; r += 32)
-                    bulk_load(vd + r * kRowBytes, vs + (int64_t)r * a.v_pstride, kRowBytes, &full[st], pol);
+                tma_load_3d(kd, &a.kmap, 0, h, row, &full[st], pol);
+                tma_load_3d(vd, &a.vmap, 0, h, row, &full[st], pol);
             }
             issued = t + 1;
         }
-        if (!ok && lane == 0) atomicOr(a.ws_status, kDevStatusTimeout);
+        if (!ok) atomicOr(a.ws_status, kDevStatusTimeout);
         // Do not leave while copies into this CTA's shared memory are in flight.
         for (int t = max(0, issued - kStages); t < issued; ++t) mbar_wait(&full[t % kStages], (t / kStages) & 1);
         return;
@@ -195,29 +281,39 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 
     // ======================= consumer warps =======================
     const int c = warp;
-    const int slot = lane >> 3;  // key within the group of 4 this step handles
+    const int slot = lane >> 3;  // key within the group of 4 a step handles
     const int g = lane & 7;      // pairs 8g .. 8g+7 (dims 8g..8g+7 and 64+8g..64+8g+7)
     const int hh = g >> 1;       // Q head whose score this lane holds after the reduction
     const int qpos = d.query_position;
 
-    if (a.mask_out != nullptr && split == 0 && h == 0) {
-        const int n_pad = ((d.seq_len + a.kv_block_len - 1) / a.kv_block_len) * a.kv_block_len;
-        for (int p = threadIdx.x; p < n_pad; p += kConsumerThreads)
-            a.mask_out[(int64_t)b * a.mask_stride + p] = key_valid(p, d.seq_len, qpos) ? 1 : 0;
+    // Q rows of the group; the loads are issued before the table work they overlap.
+    uint4 qx[kGroup], qy[kGroup];
+#pragma unroll
+    for (int hq = 0; hq < kGroup; ++hq) {
+        const __nv_bfloat16* qrow = a.q + (int64_t)b * a.q_bstride + (int64_t)(h * kGroup + hq) * a.q_hstride;
+        qx[hq] = *reinterpret_cast<const uint4*>(qrow + 8 * g);
+        qy[hq] = *reinterpret_cast<const uint4*>(qrow + kPairs + 8 * g);
     }
 
-    // Q rows of the group, rotated at QUERY_POSITION and pre-scaled by scale*log2(e).
+    if (a.mask_out != nullptr && split == 0 && h == 0) {
+        const int n_pad = ((d.seq_len + a.kv_block_len - 1) / a.kv_block_len) * a.kv_block_len;
+        for (int p = tid; p < n_pad; p += kConsumerThreads)
+            a.mask_out[(int64_t)b * a.mask_stride + p] = key_valid(p, d.seq_len, qpos) ? 1 : 0;
+    }
+    if (!single) {
+        build_rope_table(steps, rope, qpos, first_pos, tid);
+        named_barrier_sync(1, kConsumerThreads);
+    }
+
+    // Q rotated at QUERY_POSITION and pre-scaled by scale*log2(e).
     float2 qr[kGroup][4], qi[kGroup][4];
     {
         float2 wr[4], wi[4];
-        rope_factors8(a, g, qpos, wr, wi);
+        rope_row8(rope + kRopeQ * kPairs, g, wr, wi);
 #pragma unroll
         for (int hq = 0; hq < kGroup; ++hq) {
-            const __nv_bfloat16* qrow = a.q + (int64_t)b * a.q_bstride + (int64_t)(h * kGroup + hq) * a.q_hstride;
-            const uint4 xr = *reinterpret_cast<const uint4*>(qrow + 8 * g);
-            const uint4 xi = *reinterpret_cast<const uint4*>(qrow + kPairs + 8 * g);
-            const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
-            const uint32_t yw[4] = {xi.x, xi.y, xi.z, xi.w};
+            const uint32_t xw[4] = {qx[hq].x, qx[hq].y, qx[hq].z, qx[hq].w};
+            const uint32_t yw[4] = {qy[hq].x, qy[hq].y, qy[hq].z, qy[hq].w};
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
                 float2 re, im;
@@ -228,18 +324,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         }
     }
 
-    // RoPE factors of this lane's key in step 0 of the current tile, and the
-    // fixed rotations that advance them by 4 keys and by one tile.
+    // RoPE factors of this lane's key in step 0 of the current tile
+    // (first key x warp offset x slot offset).
     float2 wr[4], wi[4], sr[4], si[4], tr[4], ti[4];
-    rope_factors8(a, g, first_pos + c * kKeysPerWarp + slot, wr, wi);
+    {
+        float2 br[4], bi[4], cr[4], ci[4], xr[4], xi[4];
+        rope_row8(rope + kRopeStep * kPairs, g, sr, si);
+        rope_row8(rope + kRopeTile * kPairs, g, tr, ti);
+        rope_row8(rope + kRopeBase * kPairs, g, br, bi);
+        rope_row8(rope + (kRopeWarp + c) * kPairs, g, cr, ci);
+        rope_row8(rope + (kRopeSlot + slot) * kPairs, g, xr, xi);
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-        const float2 s0 = a.rot_step[8 * g + 2 * jj], s1 = a.rot_step[8 * g + 2 * jj + 1];
-        const float2 t0 = a.rot_tile[8 * g + 2 * jj], t1 = a.rot_tile[8 * g + 2 * jj + 1];
-        sr[jj] = make_float2(s0.x, s1.x);
-        si[jj] = make_float2(s0.y, s1.y);
-        tr[jj] = make_float2(t0.x, t1.x);
-        ti[jj] = make_float2(t0.y, t1.y);
+        for (int jj = 0; jj < 4; ++jj) {
+            float2 tr0, ti0;
+            cmul2(br[jj], bi[jj], cr[jj], ci[jj], tr0, ti0);
+            cmul2(tr0, ti0, xr[jj], xi[jj], wr[jj], wi[jj]);
+        }
     }
 
     float m_run = -INFINITY;  // running max (log2 units) of head hh
@@ -247,36 +347,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     float2 acc0[kGroup], acc1[kGroup];  // dims (4*lane, +1) and (4*lane+2, +3) of each head
 #pragma unroll
     for (int hq = 0; hq < kGroup; ++hq) acc0[hq] = acc1[hq] = make_float2(0.f, 0.f);
-    float* pw = pbuf + c * (kKeysPerWarp * kGroup);
+    // Per-warp double buffer of probabilities [2][keys][4 heads] as (p, p) pairs, and rescales [2][4].
+    float2* pw = pbuf + c * 2 * (kKeysPerWarp * kGroup);
+    float* aw = abuf + c * 2 * kGroup;
 
-    bool ok = true;
-    for (int t = 0; t < n_tiles; ++t) {
-        const int st = t % kStages;
-        if (!mbar_wait(&full[st], (t / kStages) & 1)) {
-            ok = false;
-            break;
-        }
-        const uint8_t* kt = smem + st * kStageBytes;
-        const uint8_t* vt = kt + kTileBytes;
+    // Scores of this warp's keys of tile t: RoPE of K, Q.K for the 4 heads,
+    // reduction over the 8 lanes of each key.  Keys [key0, key0 + cnt) all
+    // satisfy key_valid() (they lie in [0, min(SEQ_LEN, QUERY_POSITION + 1)));
+    // rows past them are masked.
+    auto qk_tile = [&](int t, float (&sc)[kSteps]) {
+        const uint8_t* kt = smem + (t % kStages) * kStageBytes;
         const int rows = min(kTileKeys, cnt - t * kTileKeys);
-        const int64_t tile_pos = first_pos + (int64_t)t * kTileKeys;
-
-        float sc[2];
 #pragma unroll
-        for (int step = 0; step < 2; ++step) {
+        for (int step = 0; step < kSteps; ++step) {
             const int r = c * kKeysPerWarp + step * 4 + slot;
+            const uint4 kre = *reinterpret_cast<const uint4*>(kt + r * kRowBytes + g * 16);
+            const uint4 kim = *reinterpret_cast<const uint4*>(kt + r * kRowBytes + 128 + g * 16);
             float2 ur[4], ui[4];
+            if (step == 0) {
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                if (step == 0) {
+                for (int jj = 0; jj < 4; ++jj) {
                     ur[jj] = wr[jj];
                     ui[jj] = wi[jj];
-                } else {
-                    cmul2(wr[jj], wi[jj], sr[jj], si[jj], ur[jj], ui[jj]);
                 }
+            } else {
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) cmul2(wr[jj], wi[jj], sr[jj], si[jj], ur[jj], ui[jj]);
             }
-            const uint4 kre = lds128(kt + r * kRowBytes + g * 16);
-            const uint4 kim = lds128(kt + r * kRowBytes + 128 + g * 16);
             const uint32_t xw[4] = {kre.x, kre.y, kre.z, kre.w};
             const uint32_t yw[4] = {kim.x, kim.y, kim.z, kim.w};
             float2 rr[4], ri[4];
@@ -295,19 +392,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 }
                 s[hq] = acc.x + acc.y;
             }
-            // Sum the 4 head scores over the 8 lanes of this key (lane bits 0..2);
-            // lane ends with head hh = (bit2, bit1).
             const bool b2 = lane & 4, b1 = lane & 2;
             const float t0 = (b2 ? s[2] : s[0]) + __shfl_xor_sync(0xffffffffu, b2 ? s[0] : s[2], 4);
             const float t1 = (b2 ? s[3] : s[1]) + __shfl_xor_sync(0xffffffffu, b2 ? s[1] : s[3], 4);
             float u = (b1 ? t1 : t0) + __shfl_xor_sync(0xffffffffu, b1 ? t0 : t1, 2);
             u += __shfl_xor_sync(0xffffffffu, u, 1);
-            const bool valid = r < rows && key_valid(tile_pos + r, d.seq_len, qpos);
-            sc[step] = valid ? u : -INFINITY;
+            sc[step] = r < rows ? u : -INFINITY;
         }
         // Advance the lane's RoPE factors by one tile (exactly every kReanchorTiles).
         if (((t + 1) % kReanchorTiles) == 0) {
-            rope_factors8(a, g, tile_pos + kTileKeys + c * kKeysPerWarp + slot, wr, wi);
+            rope_exact8(steps, g, first_pos + (int64_t)(t + 1) * kTileKeys + c * kKeysPerWarp + slot, wr, wi);
         } else {
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
@@ -317,55 +411,106 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 wi[jj] = ni;
             }
         }
+    };
 
-        // Online softmax for head hh over this warp's 8 keys.
-        float mx = fmaxf(sc[0], sc[1]);
+    // Online softmax of head hh over this warp's keys; publishes p and the rescale.
+    auto softmax_publish = [&](const float (&sc)[kSteps], int buf) {
+        float mx = sc[0];
+#pragma unroll
+        for (int step = 1; step < kSteps; ++step) mx = fmaxf(mx, sc[step]);
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
         const float m_new = fmaxf(m_run, mx);
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
         const float alpha = exp2f(m_run - m_use);
-        const float p0 = exp2f(sc[0] - m_use);
-        const float p1 = exp2f(sc[1] - m_use);
-        l_run = l_run * alpha + (p0 + p1);
+        float psum = 0.f;
+        float pv[kSteps];
+#pragma unroll
+        for (int step = 0; step < kSteps; ++step) {
+            pv[step] = exp2f(sc[step] - m_use);
+            psum += pv[step];
+        }
+        l_run = l_run * alpha + psum;
         m_run = m_new;
+        float2* pb = pw + buf * (kKeysPerWarp * kGroup);
         if ((g & 1) == 0) {
-            pw[slot * kGroup + hh] = p0;
-            pw[(4 + slot) * kGroup + hh] = p1;
-            if (slot == 0) abuf[c * kGroup + hh] = alpha;
+#pragma unroll
+            for (int step = 0; step < kSteps; ++step) pb[(step * 4 + slot) * kGroup + hh] = f2(pv[step]);
+            if (slot == 0) aw[buf * kGroup + hh] = alpha;
         }
         __syncwarp();
-        const float4 al = lds128f(abuf + c * kGroup);
+    };
+
+    // acc = acc * alpha + sum_k p_k * V_k over this warp's keys of tile t.
+    auto pv_tile = [&](int t, int buf) {
+        uint8_t* vt = smem + (t % kStages) * kStageBytes + kTileBytes;
+        const int nr = min(kTileKeys, cnt - t * kTileKeys) - c * kKeysPerWarp;
+        if (nr < kKeysPerWarp) {
+            // Last tile of the split: rows past its keys may hold anything (even
+            // NaN).  Their probabilities are 0; zero their values too.
+            for (int rr = max(nr, 0); rr < kKeysPerWarp; ++rr)
+                *reinterpret_cast<uint2*>(vt + (c * kKeysPerWarp + rr) * kRowBytes + lane * 8) = make_uint2(0u, 0u);
+            __syncwarp();
+        }
+        const float2* pb = pw + buf * (kKeysPerWarp * kGroup);
+        const float4 al = *reinterpret_cast<const float4*>(aw + buf * kGroup);
         const float alv[4] = {al.x, al.y, al.z, al.w};
 #pragma unroll
         for (int hq = 0; hq < kGroup; ++hq) {
             acc0[hq] = __fmul2_rn(acc0[hq], f2(alv[hq]));
             acc1[hq] = __fmul2_rn(acc1[hq], f2(alv[hq]));
         }
-        const int nr = rows - c * kKeysPerWarp;  // keys of this warp present in the tile
 #pragma unroll
         for (int rr = 0; rr < kKeysPerWarp; ++rr) {
-            if (rr < nr) {
-                const float4 pp = lds128f(pw + rr * kGroup);
-                const uint2 vv = lds64(vt + (c * kKeysPerWarp + rr) * kRowBytes + lane * 8);
-                const float2 v0 = bf16x2_to_float2(vv.x), v1 = bf16x2_to_float2(vv.y);
-                const float pv[4] = {pp.x, pp.y, pp.z, pp.w};
+            const float4 p01 = *reinterpret_cast<const float4*>(pb + rr * kGroup);
+            const float4 p23 = *reinterpret_cast<const float4*>(pb + rr * kGroup + 2);
+            const uint2 vv = *reinterpret_cast<const uint2*>(vt + (c * kKeysPerWarp + rr) * kRowBytes + lane * 8);
+            const float2 v0 = bf16x2_to_float2(vv.x), v1 = bf16x2_to_float2(vv.y);
+            const float2 pk[4] = {make_float2(p01.x, p01.y), make_float2(p01.z, p01.w), make_float2(p23.x, p23.y),
+                                  make_float2(p23.z, p23.w)};
 #pragma unroll
-                for (int hq = 0; hq < kGroup; ++hq) {
-                    acc0[hq] = __ffma2_rn(f2(pv[hq]), v0, acc0[hq]);
-                    acc1[hq] = __ffma2_rn(f2(pv[hq]), v1, acc1[hq]);
-                }
+            for (int hq = 0; hq < kGroup; ++hq) {
+                acc0[hq] = __ffma2_rn(pk[hq], v0, acc0[hq]);
+                acc1[hq] = __ffma2_rn(pk[hq], v1, acc1[hq]);
             }
         }
+    };
+
+    // Software pipeline: the P.V of tile t-1 is issued in the same block as
+    // the Q.K of tile t, giving each warp two independent instruction streams.
+    bool ok = true;
+    if (n_tiles > 0) {
+        if (mbar_wait(&full[0], 0)) {
+            float sc[kSteps];
+            qk_tile(0, sc);
+            softmax_publish(sc, 0);
+        } else {
+            ok = false;
+        }
+    }
+    for (int t = 1; t < n_tiles && ok; ++t) {
+        if (!mbar_wait(&full[t % kStages], (t / kStages) & 1)) {
+            ok = false;
+            break;
+        }
+        float sc[kSteps];
+        qk_tile(t, sc);
+        pv_tile(t - 1, (t - 1) & 1);
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
+        if (lane == 0) mbar_arrive(&empty[(t - 1) % kStages]);
+        softmax_publish(sc, t & 1);
+    }
+    if (ok && n_tiles > 0) {
+        pv_tile(n_tiles - 1, (n_tiles - 1) & 1);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[(n_tiles - 1) % kStages]);
     }
     if (!ok && lane == 0) atomicOr(a.ws_status, kDevStatusTimeout);
 
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 8);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);
 
-    // ---- merge the 8 warps through shared memory (the ring is free now)
+    // ---- merge the warps through shared memory (the ring is free now)
     named_barrier_sync(1, kConsumerThreads);
     float* cb = reinterpret_cast<float*>(smem);
     {
@@ -381,75 +526,96 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
     named_barrier_sync(1, kConsumerThreads);
 
-    const int tid = threadIdx.x;
-    const int dim = tid & 127;
-    float res_acc[2], res_m[2], res_l[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int hq = (tid >> 7) + 2 * i;
+    const OutSpec direct{a.out, a.o_bstride, a.o_hstride, a.flags};
+    float* part = a.ws_partials + ((int64_t)gsplit * kNumKVHeads + h) * kGroup * kPartialFloats;
+    for (int o = tid; o < kOutputs; o += kConsumerThreads) {
+        const int hq = o >> 7, dim = o & 127;
+        float mw[kConsumerWarps];
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cb[(w * kGroup + hq) * kPartialFloats + 128]);
+        for (int w = 0; w < kConsumerWarps; ++w) {
+            mw[w] = cb[(w * kGroup + hq) * kPartialFloats + 128];
+            M = fmaxf(M, mw[w]);
+        }
         const float Mu = M == -INFINITY ? 0.f : M;
         float L = 0.f, O = 0.f;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) {
             const float* row = cb + (w * kGroup + hq) * kPartialFloats;
-            const float f = exp2f(row[128] - Mu);
+            const float f = exp2f(mw[w] - Mu);
             L = fmaf(row[129], f, L);
             O = fmaf(row[dim], f, O);
         }
-        res_acc[i] = O;
-        res_m[i] = M;
-        res_l[i] = L;
+        if (n_split == 1) {
+            write_result(direct, b, h * kGroup + hq, dim, O, M, L);
+        } else {
+            float* row = part + hq * kPartialFloats;
+            row[dim] = O;
+            if (dim == 0) {
+                row[128] = M;
+                row[129] = L;
+            }
+        }
     }
+}
 
-    if (n_split == 1) {
-#pragma unroll
-        for (int i = 0; i < 2; ++i) write_result(a, b, h * kGroup + (tid >> 7) + 2 * i, dim, res_acc[i], res_m[i], res_l[i]);
-        return;
-    }
+// ---------------------------------------------------------------------------
+// Merge of a sequence's split partials: one CTA per (sequence, Q head), one
+// thread per dim.  Runs after decode_kernel (griddepcontrol.wait).
+// ---------------------------------------------------------------------------
+struct MergeArgs {
+    const float* partials;  // [total_splits][32][132]
+    const int2* seqinfo;    // [batch]: (first global split, splits) of sequences with > 1 split
+    const SeqDesc* descs;   // nullptr: single sequence, splits from `single_splits`
+    int single_splits;
+    int chunk;
+    OutSpec out;
+};
 
-    // ---- publish this split's partial; the last split of (b, h) merges them
-    float* part = a.ws_partials + ((int64_t)gsplit * kNumKVHeads + h) * kGroup * kPartialFloats;
+__global__ void __launch_bounds__(kHeadDim) split_merge_kernel(const __grid_constant__ MergeArgs m) {
+    __shared__ float fac[kMaxSplitsPerSeq];
+    __shared__ float red[2][4];
+    allow_dependent_launch();
+    const int b = blockIdx.x / kNumQHeads;
+    const int qh = blockIdx.x % kNumQHeads;
+    const int dim = threadIdx.x;
+    grid_dependency_wait();
+    const int n_split = m.descs == nullptr ? m.single_splits : seq_splits(m.descs[b], m.chunk);
+    if (n_split <= 1) return;  // written directly by decode_kernel
+    const int2 si = m.seqinfo[b];
+    const int64_t split_stride = (int64_t)kNumQHeads * kPartialFloats;
+    const float* base = m.partials + ((int64_t)si.x * kNumQHeads + qh) * kPartialFloats;
+    // Split s's max and sum (threads s < n_split), block max and weighted sum.
+    float ms = -INFINITY, ls = 0.f;
+    if (dim < n_split) {
+        ms = __ldcg(base + dim * split_stride + 128);
+        ls = __ldcg(base + dim * split_stride + 129);
+    }
+    float M = ms;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        float* row = part + ((tid >> 7) + 2 * i) * kPartialFloats;
-        row[dim] = res_acc[i];
-        if (dim == 0) {
-            row[128] = res_m[i];
-            row[129] = res_l[i];
-        }
-    }
-    __threadfence();
-    named_barrier_sync(1, kConsumerThreads);
-    if (tid == 0) {
-        const unsigned old = atomicAdd(&a.ws_counters[b * kNumKVHeads + h], 1u);
-        info[2] = old == (unsigned)(n_split - 1) ? 1 : 0;
-    }
-    named_barrier_sync(1, kConsumerThreads);
-    if (info[2] == 0) return;
-    __threadfence();
-    const int gbase = gsplit - split;
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if ((dim & 31) == 0) red[0][dim >> 5] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+    const float Mu = M == -INFINITY ? 0.f : M;
+    const float f = dim < n_split ? exp2f(ms - Mu) : 0.f;
+    if (dim < n_split) fac[dim] = f;
+    float L = ls * f;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int hq = (tid >> 7) + 2 * i;
-        float M = -INFINITY;
-        for (int s = 0; s < n_split; ++s) {
-            const float* row = a.ws_partials + (((int64_t)(gbase + s) * kNumKVHeads + h) * kGroup + hq) * kPartialFloats;
-            M = fmaxf(M, __ldcg(row + 128));
-        }
-        const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f, O = 0.f;
-        for (int s = 0; s < n_split; ++s) {
-            const float* row = a.ws_partials + (((int64_t)(gbase + s) * kNumKVHeads + h) * kGroup + hq) * kPartialFloats;
-            const float f = exp2f(__ldcg(row + 128) - Mu);
-            L = fmaf(__ldcg(row + 129), f, L);
-            O = fmaf(__ldcg(row + dim), f, O);
-        }
-        write_result(a, b, h * kGroup + hq, dim, O, M, L);
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if ((dim & 31) == 0) red[1][dim >> 5] = L;
+    __syncthreads();
+    L = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
+    float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < n_split; s0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = s0 + j < n_split ? __ldcg(base + (s0 + j) * split_stride + dim) : 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o8[j] = fmaf(v[j], s0 + j < n_split ? fac[s0 + j] : 0.f, o8[j]);
     }
-    if (tid == 0) a.ws_counters[b * kNumKVHeads + h] = 0u;
+    const float O = ((o8[0] + o8[1]) + (o8[2] + o8[3])) + ((o8[4] + o8[5]) + (o8[6] + o8[7]));
+    write_result(m.out, b, qh, dim, O, M, L);
 }
 
 // ---------------------------------------------------------------------------
@@ -502,9 +668,24 @@ __global__ void __launch_bounds__(256) rope_rows_kernel(const __nv_bfloat16* __r
     }
 }
 
+cudaError_t launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, func, args);
+}
+
 }  // namespace
 
 int decode_tile_keys() { return kTileKeys; }
+int decode_max_splits() { return kMaxSplitsPerSeq; }
 size_t decode_smem_bytes() { return kSmemBytes; }
 
 cudaError_t decode_prepare(int device) {
@@ -512,9 +693,21 @@ cudaError_t decode_prepare(int device) {
     return cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
 }
 
-cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t stream) {
-    decode_kernel<<<grid, kThreads, kSmemBytes, stream>>>(a);
-    return cudaGetLastError();
+cudaError_t launch_decode(const DecodeArgs& a, int grid, int total_splits, cudaStream_t stream) {
+    void* dargs[] = {const_cast<DecodeArgs*>(&a)};
+    cudaError_t e = launch_pdl(reinterpret_cast<const void*>(decode_kernel), dim3(grid), dim3(kThreads), kSmemBytes,
+                               stream, dargs);
+    if (e != cudaSuccess || total_splits <= a.batch) return e;  // every sequence had one split
+    MergeArgs m;
+    m.partials = a.ws_partials;
+    m.seqinfo = a.ws_seqinfo;
+    m.descs = a.descs;
+    m.single_splits = a.descs == nullptr ? total_splits : 0;
+    m.chunk = a.chunk;
+    m.out = OutSpec{a.out, a.o_bstride, a.o_hstride, a.flags};
+    void* margs[] = {&m};
+    return launch_pdl(reinterpret_cast<const void*>(split_merge_kernel), dim3(a.batch * kNumQHeads), dim3(kHeadDim), 0,
+                      stream, margs);
 }
 
 cudaError_t launch_combine(const float* parts, int n_parts, int64_t part_stride, int64_t batch_stride, int batch,

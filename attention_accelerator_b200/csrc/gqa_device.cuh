@@ -3,6 +3,7 @@
 // wrappers with bounded waits, BF16 unpacking and the RoPE phase generator.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -54,7 +55,12 @@ __host__ __device__ inline bool key_valid(int64_t p, int seq_len, int query_posi
     return p < seq_len && p <= query_position;
 }
 
-struct DecodeArgs {
+// Kernel argument block, passed by value as a __grid_constant__ parameter.  The
+// two tensor maps come first: TMA requires them 64-byte aligned in param space.
+struct alignas(64) DecodeArgs {
+    CUtensorMap kmap;       // K rows: 3-D (dim, row, head) or (dim, head, row), box = one tile of one head
+    CUtensorMap vmap;
+    int kv_rows_inner;      // 1: rows are tensor-map dimension 1 (head-major), 0: dimension 2
     const __nv_bfloat16* q;
     const __nv_bfloat16* k;
     const __nv_bfloat16* v;
@@ -70,7 +76,7 @@ struct DecodeArgs {
     float qscale;           // scale * log2(e): scores are kept in log2 units
     uint32_t flags;         // GQA_FLAG_*
     uint32_t* ws_status;
-    uint32_t* ws_counters;  // [batch][8] split counters, self-resetting
+    int2* ws_seqinfo;       // [batch]: (first global split, splits) of sequences with > 1 split
     float* ws_partials;     // [total_splits][8][4][132]
     uint8_t* mask_out;
     int64_t mask_stride;
@@ -132,6 +138,22 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
     return pol;
+}
+
+// Tiled TMA copy of one box of a 3-D tensor map into this CTA's shared memory,
+// completing the box's bytes of transaction count on `bar`.  The innermost
+// coordinate is always 0 (head_dim starts a row), so it is 16-byte aligned.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, uint64_t* bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 // Bulk (non-tensor) TMA copy global -> this CTA's shared memory, completing

@@ -10,9 +10,10 @@ namespace gqa {
 struct DecodeArgs;
 
 int decode_tile_keys();
+int decode_max_splits();
 size_t decode_smem_bytes();
 cudaError_t decode_prepare(int device);
-cudaError_t launch_decode(const DecodeArgs& a, int grid, cudaStream_t stream);
+cudaError_t launch_decode(const DecodeArgs& a, int grid, int total_splits, cudaStream_t stream);
 cudaError_t launch_combine(const float* parts, int n_parts, int64_t part_stride, int64_t batch_stride, int batch,
                            void* out, int64_t o_bstride, int64_t o_hstride, cudaStream_t stream);
 cudaError_t launch_rope_rows(const void* x, const int32_t* pos, float* out, int rows, const uint64_t* step,

@@ -125,7 +125,7 @@ class Workload:
 class SingleDecode(Workload):
     """One sequence per step per GPU; rotating buffer sets beat the L2."""
 
-    def __init__(self, device, rank, seq_len, qpos, uniform=False, seed=20260805):
+    def __init__(self, device, rank, seq_len, qpos, uniform=False, seed=20260805, layout="position_major"):
         import torch
         import attention_accelerator_b200 as gqa
         self.gqa, self.torch = gqa, torch
@@ -143,9 +143,11 @@ class SingleDecode(Workload):
                 return (torch.rand(shape, generator=g, device=device) * 2 - 1).to(torch.bfloat16)
             return torch.randn(shape, generator=g, device=device).to(torch.bfloat16)
 
+        self.layout = layout
+        kv_shape = (seq_len, 8, 128) if layout == "position_major" else (8, seq_len, 128)
         self.q = [rnd((32, 128)) for _ in range(self.nsets)]
-        self.k = [rnd((seq_len, 8, 128)) for _ in range(self.nsets)]
-        self.v = [rnd((seq_len, 8, 128)) for _ in range(self.nsets)]
+        self.k = [rnd(kv_shape) for _ in range(self.nsets)]
+        self.v = [rnd(kv_shape) for _ in range(self.nsets)]
         self.out = torch.empty((32, 128), dtype=torch.bfloat16, device=device)
         self.l2_note = (f"{self.nsets} rotating buffer sets of {per_set / 2**20:.1f} MiB "
                         f"({self.nsets * per_set / 2**20:.0f} MiB > 2x L2)")
@@ -156,11 +158,13 @@ class SingleDecode(Workload):
 
     def launch(self, i):
         j = i % self.nsets
-        self.gqa.decode(self.q[j], self.k[j], self.v[j], seq_len=self.S, query_position=self.qpos, out=self.out)
+        self.gqa.decode(self.q[j], self.k[j], self.v[j], seq_len=self.S, query_position=self.qpos, out=self.out,
+                        layout=self.layout)
 
     def config(self):
+        lay = "position_major [S,8,128]" if self.layout == "position_major" else "head_major [8,S,128]"
         return {"workload": self.name, "batch_per_gpu": 1, "seq_len": self.S, "query_position": self.qpos,
-                "kv_block_len": 16, "kv_layout": "position_major [S,8,128] bf16", "l2": self.l2_note}
+                "kv_block_len": 16, "kv_layout": f"{lay} bf16", "l2": self.l2_note}
 
     def e2e_inputs(self):
         t = self.torch
@@ -168,7 +172,7 @@ class SingleDecode(Workload):
 
     def e2e_step(self, host):
         q, k, v = host
-        return self.gqa.decode(q, k, v, seq_len=self.S, query_position=self.qpos)
+        return self.gqa.decode(q, k, v, seq_len=self.S, query_position=self.qpos, layout=self.layout)
 
     def oracle_inputs(self):
         """Head-major BF16 codes of buffer set 0 for the CPU restatement."""
@@ -177,8 +181,10 @@ class SingleDecode(Workload):
 
         def bits(x):
             return x.contiguous().view(t.int16).cpu().numpy().astype(np.uint16)
-        return (bits(self.q[0]), bits(self.k[0].transpose(0, 1)), bits(self.v[0].transpose(0, 1)),
-                self.S, self.qpos)
+        k, v = self.k[0], self.v[0]
+        if self.layout == "position_major":
+            k, v = k.transpose(0, 1), v.transpose(0, 1)
+        return bits(self.q[0]), bits(k), bits(v), self.S, self.qpos
 
     def gpu_result_set0(self):
         import numpy as np
@@ -325,11 +331,11 @@ class LongContext(Workload):
         return None
 
 
-def make_workload(name, device, rank, world):
+def make_workload(name, device, rank, world, layout="position_major"):
     if name == "config1":
-        return SingleDecode(device, rank, 30, 29, uniform=True)
+        return SingleDecode(device, rank, 30, 29, uniform=True, layout=layout)
     if name == "config2":
-        return SingleDecode(device, rank, 4096, 4095)
+        return SingleDecode(device, rank, 4096, 4095, layout=layout)
     if name == "config3":
         return RaggedBatch(device, rank)
     if name == "config4":
@@ -497,6 +503,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("config1", "config2", "config3", "config4"), default="config2")
+    ap.add_argument("--layout", choices=("position_major", "head_major"), default="position_major")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -521,7 +528,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
         build_library()
-    wl = make_workload(args.workload, device, rank, world)
+    wl = make_workload(args.workload, device, rank, world, args.layout)
     stream = torch.cuda.Stream(device)
     sampler = ClockSampler(local) if rank == 0 else None
     ms, window = timed_graph_run(torch, wl, args.steps, args.warmup, stream, dist_on)
