@@ -136,8 +136,9 @@ int gqa_validate(const gqa_params *p);
  * Bytes of device workspace a call needs (0 on invalid input).  `descs` is the
  * host copy of the batch's descriptors, or NULL with batch == 1 for a
  * single-sequence call described by p->seq_len / p->query_position.
- * The workspace must be zero-filled once when it is allocated; every call
- * leaves it zeroed again (its split counters reset themselves).
+ * The workspace's first 4 bytes (the device status word) must be zero when it
+ * is allocated; the rest needs no initialisation (every call writes its split
+ * partials before reading them).
  */
 size_t gqa_workspace_bytes(const gqa_params *p, const gqa_seq_desc *descs, int batch);
 
