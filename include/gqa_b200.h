@@ -154,6 +154,28 @@ int gqa_decode(const void *q, const void *k, const void *v, void *out,
                const gqa_params *p, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * gqa_decode without a workspace argument: no counterpart in the reference.
+ * For callers that may not allocate device memory (a plug-in inside a host
+ * program that owns every device allocation, or a loop that cannot afford
+ * cudaMalloc's implicit synchronisation), the split table and partials live in
+ * a library-owned device array of GQA_NOALLOC_SCRATCH_BYTES; each GPU that
+ * loads the library holds that array until the process exits.  Nothing is
+ * allocated or freed by this call.
+ *  - The first call on a device looks up the array's device address for that
+ *    device (cudaGetSymbolAddress); make that first call before any stream
+ *    capture begins.
+ *  - A call whose scratch would exceed GQA_NOALLOC_SCRATCH_BYTES returns
+ *    GQA_ERR_WORKSPACE without launching; use gqa_decode with a workspace.
+ *  - All calls on a device share the one array and it keeps the last call's
+ *    contents: calls whose kernels overlap on the GPU (several streams, or
+ *    several host threads) race and corrupt each other's results; serialise
+ *    them.  In-kernel wait timeouts are not reported on this path.
+ */
+#define GQA_NOALLOC_SCRATCH_BYTES ((size_t)1 << 20)
+int gqa_decode_noalloc(const void *q, const void *k, const void *v, void *out,
+                       const gqa_params *p, void *stream);
+
+/*
  * Batched (ragged) decode: one query token per sequence, B sequences.  The
  * per-sequence register values come from `descs`; `host_descs` is the same
  * array in host memory (used to validate and plan), `dev_descs` in device
