@@ -265,7 +265,8 @@ class LongContext(Workload):
         self.scaling = "strong"
         self.bytes_per_step = kv_bytes(seq_len)  # whole job; each rank reads 1/world of the keys
         self.qheads_per_step = 32
-        lo, hi = rank * seq_len // world, (rank + 1) * seq_len // world
+        from attention_accelerator_b200.distributed import shard_range
+        lo, hi = shard_range(seq_len, rank, world)
         self.lo, self.hi = lo, hi
         per_set = 2 * (hi - lo) * 8 * 128 * 2
         self.nsets = max(2, math.ceil(2 * L2_BYTES / per_set))
@@ -300,7 +301,7 @@ class LongContext(Workload):
         import torch.distributed as dist
         self.gqa.decode_batch(self.q[j], self.k[j], self.v[j], self.plan, out=self.part)
         dist.all_gather_into_tensor(self.gathered.view(self.world, -1), self.part.view(-1))
-        self.gqa.combine_partials(self.gathered, out=self.out)
+        self.gqa.combine_partials(self.gathered, out=self.out)  # same as distributed.gather_partials + combine
 
     def config(self):
         return {"workload": self.name, "batch": 1, "seq_len": self.S, "query_position": self.S - 1,
@@ -317,11 +318,9 @@ class LongContext(Workload):
         if self.world == 1:
             out = self.gqa.decode(q[0], k, v, seq_len=self.S, query_position=self.S - 1)
         else:
-            import torch.distributed as dist
+            from attention_accelerator_b200.distributed import gather_partials
             part = self.gqa.decode_batch(q, k, v, self.plan)
-            gathered = self.torch.empty((self.world,) + tuple(part.shape), dtype=part.dtype, device=dev)
-            dist.all_gather_into_tensor(gathered.view(self.world, -1), part.view(-1))
-            out = self.gqa.combine_partials(gathered)
+            out = self.gqa.combine_partials(gather_partials(part))
         return out.cpu()
 
     def oracle_inputs(self):

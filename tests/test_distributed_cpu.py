@@ -1,0 +1,95 @@
+"""Multi-rank host logic on CPU: world-size-2 ``gloo`` process groups.
+
+The GPU kernels are replaced here by the oracle's float64 partials (this is a
+test of the decomposition and the collective plumbing, not of the kernels,
+which tests/test_decode_gpu.py covers): each rank computes the partial of its
+contiguous key shard, ``gather_partials`` all-gathers them over gloo, and the
+log-sum-exp merge must reproduce the single-process golden.  Sequence
+sharding is checked for coverage and balance.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from attention_accelerator_b200.distributed import balance_sequences, gather_partials, shard_range
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _inputs(seq_len: int, seed: int):
+    g = torch.Generator().manual_seed(seed)
+
+    def bits(t):
+        return t.to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint16)
+    return (bits(torch.randn(32, 128, generator=g)), bits(torch.randn(8, seq_len, 128, generator=g)),
+            bits(torch.randn(8, seq_len, 128, generator=g)))
+
+
+def _worker(rank: int, world: int, port: int, seq_len: int, qpos: int, result_q):
+    from oracle.partials import combine_f64, from_rows, partial_f64, to_rows
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, k, v = _inputs(seq_len, seed=7)
+        lo, hi = shard_range(seq_len, rank, world)
+        local = torch.from_numpy(to_rows(*partial_f64(q, k, v, qpos, lo, hi)).astype(np.float32))[None]
+        gathered = gather_partials(local)  # [world, 1, 32, 132]
+        parts = [from_rows(gathered[r, 0].numpy()) for r in range(world)]
+        result_q.put((rank, combine_f64(parts)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("seq_len,qpos", [(300, 299), (300, 120)])
+def test_sequence_split_over_gloo_matches_single_process(seq_len, qpos):
+    from oracle import check_rows, gqa_golden
+    world = 2
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, seq_len, qpos, result_q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(result_q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    q, k, v = _inputs(seq_len, seed=7)
+    golden = gqa_golden(q, k, v, seq_len, qpos, exact=False)
+    for r in range(world):
+        res = check_rows(golden, results[r], 64)
+        assert res.passed and res.worst_ulp <= 1, res.line()
+    np.testing.assert_array_equal(results[0], results[1])
+
+
+def test_shard_ranges_cover_exactly():
+    for n in (1, 7, 131072, 131071):
+        for world in (1, 2, 4, 8):
+            ranges = [shard_range(n, r, world) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == n
+            assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+            sizes = [hi - lo for lo, hi in ranges]
+            assert max(sizes) - min(sizes) <= 1
+
+
+def test_balance_sequences_covers_and_balances():
+    rng = np.random.default_rng(0)
+    lens = rng.integers(512, 8193, size=64).tolist()
+    for world in (1, 2, 4, 8):
+        parts = balance_sequences(lens, world)
+        assert sorted(i for p in parts for i in p) == list(range(64))
+        loads = [sum(lens[i] for i in p) for p in parts]
+        assert max(loads) - min(loads) <= max(lens)
+    with pytest.raises(ValueError):
+        shard_range(10, 2, 2)
