@@ -254,7 +254,9 @@ int fill_args(gqa::DecodeArgs& a, const void* q, const void* k, const void* v, v
     a.mask_out = p->mask_out;
     a.mask_stride = p->mask_stride;
     a.kv_block_len = (int)p->kv_block_len;
-    rope_steps((double)p->rope_theta, a.rope_step, a.rot_step, a.rot_tile, gqa::decode_tile_keys());
+    bool out_of_slots = false;
+    if (gqa::rope_table_for((double)p->rope_theta, &a.rope, &out_of_slots) != cudaSuccess) return GQA_ERR_CUDA;
+    if (out_of_slots) return GQA_ERR_ROPE_THETA;
     return GQA_OK;
 }
 
@@ -280,7 +282,7 @@ const char* gqa_status_string(int status) {
         case GQA_ERR_CUDA: return "CUDA runtime error";
         case GQA_ERR_DEVICE_TIMEOUT: return "a bounded wait inside a kernel timed out";
         case GQA_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 GPU";
-        case GQA_ERR_ROPE_THETA: return "invalid rope_theta";
+        case GQA_ERR_ROPE_THETA: return "invalid rope_theta, or more than 4 distinct rope_theta values on one device";
         default: return "unknown status";
     }
 }

@@ -28,15 +28,18 @@
 #include "gqa_device.cuh"
 #include "gqa_internal.h"
 
+#include <cmath>
+#include <mutex>
+
 namespace gqa {
 
 namespace {
 
 // 11 consumer warps + 1 producer warp = 12 warps: the most warps the 168
 // registers a consumer thread needs allow (64K registers per SM).
-constexpr int kConsumerWarps = 11;
-constexpr int kKeysPerWarp = 8;                             // keys of one tile per warp
-constexpr int kTileKeys = kConsumerWarps * kKeysPerWarp;    // 88 keys per pipeline tile
+constexpr int kConsumerWarps = kDecodeConsumerWarps;
+constexpr int kKeysPerWarp = kDecodeKeysPerWarp;  // keys of one tile per warp
+constexpr int kTileKeys = kDecodeTileKeys;        // 88 keys per pipeline tile
 constexpr int kStages = 4;
 constexpr int kSteps = kKeysPerWarp / 4;                  // groups of 4 keys (8 lanes per key)
 static_assert(kSteps >= 1 && kSteps * 4 == kKeysPerWarp, "a warp takes whole groups of 4 keys");
@@ -50,19 +53,16 @@ constexpr int kReanchorTiles = 32;  // exact RoPE phase every 32 tiles (2048 key
 constexpr int kOutputs = kGroup * kHeadDim;
 
 // Shared-memory layout.
-constexpr int kOffBars = kStages * kStageBytes;
-constexpr int kOffP = kOffBars + 2 * kStages * 8;
+constexpr int kOffBars = kStages * kStageBytes;       // full[kStages], empty[kStages], q
+constexpr int kOffQ = kOffBars + (2 * kStages + 2) * 8;  // the group's 4 Q rows (BF16)
+constexpr int kOffP = kOffQ + kGroup * kRowBytes;
 constexpr int kPBytes = 2 * kConsumerWarps * kKeysPerWarp * kGroup * 8;  // [warp][2][key][head] (p, p)
 constexpr int kOffAlpha = kOffP + kPBytes;
-// RoPE tables shared by the CTA's lanes (float2 each, kPairs per row): Q
-// factors at QUERY_POSITION, the CTA's first-key factors, per-warp offsets
-// e^{i theta 8c}, per-slot offsets e^{i theta s}, and the 4-key and one-tile
-// advances.
-constexpr int kRopeQ = 0, kRopeBase = 1, kRopeWarp = 2, kRopeSlot = 2 + kConsumerWarps, kRopeStep = kRopeSlot + 4,
-              kRopeTile = kRopeStep + 1, kRopeRows = kRopeTile + 1;
+// Exact RoPE factors shared by the CTA's lanes (float2, kPairs per row): Q at
+// QUERY_POSITION and the CTA's first key.
+constexpr int kRopeQ = 0, kRopeBase = 1, kRopeRows = 2;
 constexpr int kOffRope = kOffAlpha + 2 * kConsumerWarps * kGroup * 4;
-constexpr int kOffSteps = kOffRope + kRopeRows * kPairs * 8;  // u64 Q0.64 phase steps, copied from the arguments
-constexpr int kOffInfo = kOffSteps + kPairs * 8;
+constexpr int kOffInfo = kOffRope + kRopeRows * kPairs * 8;
 constexpr int kSmemBytes = kOffInfo + 64;
 static_assert(kConsumerWarps * kGroup * kPartialFloats * 4 <= kOffBars, "warp merge buffer fits the ring");
 
@@ -83,58 +83,25 @@ __device__ __forceinline__ void cmul2(float2 ar, float2 ai, float2 br, float2 bi
     ci = __ffma2_rn(ar, bi, __fmul2_rn(ai, br));
 }
 
-// Exact factors of this lane's 8 pairs (8g .. 8g+7) at absolute position pos,
-// from the shared copy of the phase steps.
-__device__ __forceinline__ void rope_exact8(const uint64_t* steps, int g, int64_t pos, float2 (&wr)[4],
+// Exact factors of this lane's 8 pairs (8g .. 8g+7) at absolute position pos.
+__device__ __forceinline__ void rope_exact8(const RopeTable* rt, int g, int64_t pos, float2 (&wr)[4],
                                             float2 (&wi)[4]) {
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
-        const float2 f0 = rope_factor(steps[8 * g + 2 * jj], pos);
-        const float2 f1 = rope_factor(steps[8 * g + 2 * jj + 1], pos);
+        const float2 f0 = rope_factor(rt->step[8 * g + 2 * jj], pos);
+        const float2 f1 = rope_factor(rt->step[8 * g + 2 * jj + 1], pos);
         wr[jj] = make_float2(f0.x, f1.x);
         wi[jj] = make_float2(f0.y, f1.y);
     }
 }
 
-// The 8 factors of pairs 8g..8g+7 from one row of the shared RoPE table.
+// The 8 factors of pairs 8g..8g+7 of one table row (shared or global memory).
 __device__ __forceinline__ void rope_row8(const float2* row, int g, float2 (&wr)[4], float2 (&wi)[4]) {
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
         const float4 f = *reinterpret_cast<const float4*>(row + 8 * g + 2 * jj);
         wr[jj] = make_float2(f.x, f.z);
         wi[jj] = make_float2(f.y, f.w);
-    }
-}
-
-// Copy the phase steps and the two fixed advances from the argument block to
-// shared memory: one load per thread, all in flight together.
-__device__ __forceinline__ void stage_rope_constants(const DecodeArgs& a, float2* rope, uint64_t* steps, int tid) {
-    if (tid < kPairs) {
-        steps[tid] = a.rope_step[tid];
-    } else if (tid < 2 * kPairs) {
-        rope[kRopeStep * kPairs + tid - kPairs] = a.rot_step[tid - kPairs];
-    } else if (tid < 3 * kPairs) {
-        rope[kRopeTile * kPairs + tid - 2 * kPairs] = a.rot_tile[tid - 2 * kPairs];
-    }
-}
-
-// Fill the exact rows of the shared RoPE table for a CTA whose Q sits at qpos
-// and whose first key is at first_pos (consumer threads, after the steps are staged).
-__device__ __forceinline__ void build_rope_table(const uint64_t* steps, float2* rope, int qpos, int64_t first_pos,
-                                                 int tid) {
-    constexpr int kExact = (2 + kConsumerWarps + 4) * kPairs;
-    constexpr int kIters = (kExact + kConsumerThreads - 1) / kConsumerThreads;
-#pragma unroll
-    for (int j = 0; j < kIters; ++j) {
-        const int f = tid + j * kConsumerThreads;
-        if (f < kExact) {
-            const int row = f / kPairs, i = f - row * kPairs;
-            const int64_t pos = row == kRopeQ      ? (int64_t)qpos
-                                : row == kRopeBase ? first_pos
-                                : row < kRopeSlot  ? (int64_t)(row - kRopeWarp) * kKeysPerWarp
-                                                   : (int64_t)(row - kRopeSlot);
-            rope[f] = rope_factor(steps[i], pos);
-        }
     }
 }
 
@@ -168,8 +135,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     float2* pbuf = reinterpret_cast<float2*>(smem + kOffP);
     float* abuf = reinterpret_cast<float*>(smem + kOffAlpha);
     float2* rope = reinterpret_cast<float2*>(smem + kOffRope);
-    uint64_t* steps = reinterpret_cast<uint64_t*>(smem + kOffSteps);
     int* info = reinterpret_cast<int*>(smem + kOffInfo);
+    const RopeTable* rt = a.rope;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -178,24 +145,47 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const int gsplit = blockIdx.x / kNumKVHeads;
     const bool single = a.descs == nullptr;
 
+    uint64_t* qbar = empty + kStages;
+    const uint8_t* qs = smem + kOffQ;
+    const int c = warp;
+    const int slot = lane >> 3;  // key within the group of 4 a step handles
+    const int g = lane & 7;      // pairs 8g .. 8g+7 (dims 8g..8g+7 and 64+8g..64+8g+7)
+    const int hh = g >> 1;       // Q head whose score this lane holds after the reduction
+
     // ---- set-up that reads only the argument block: before the dependency wait
     if (tid == kConsumerThreads) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
+        mbar_init(qbar, 1);
         fence_barrier_init();
         prefetch_tensormap(&a.kmap);
         prefetch_tensormap(&a.vmap);
     }
+    // Per-lane RoPE state: Q factors at QUERY_POSITION, the factors of this
+    // lane's key in step 0 of the first tile (first key x lane offset), and the
+    // fixed 4-key and one-tile advances.  Constant rows come from the immutable
+    // table (L2-resident after the first CTA); the two position-dependent rows
+    // are computed exactly, one factor per thread of the first 128.
+    float2 qfr[4], qfi[4], wr[4], wi[4], sr[4], si[4], tr[4], ti[4], lr[4], li[4];
     if (warp < kConsumerWarps) {
-        stage_rope_constants(a, rope, steps, tid);
-        named_barrier_sync(1, kConsumerThreads);
-        if (single) {
-            const int64_t first_pos = (int64_t)a.single.pos_begin + (int64_t)gsplit * a.chunk;
-            build_rope_table(steps, rope, a.single.query_position, first_pos, tid);
-        }
+        rope_row8(rt->rot_step, g, sr, si);
+        rope_row8(rt->rot_tile, g, tr, ti);
+        rope_row8(rt->lane_off[c * 4 + slot], g, lr, li);
     }
+    auto lane_rope = [&](int qpos, int64_t first_pos) {
+        if (tid < 2 * kPairs)
+            rope[tid] = rope_factor(rt->step[tid & (kPairs - 1)], tid < kPairs ? (int64_t)qpos : first_pos);
+        named_barrier_sync(1, kConsumerThreads);
+        rope_row8(rope + kRopeQ * kPairs, g, qfr, qfi);
+        float2 br[4], bi[4];
+        rope_row8(rope + kRopeBase * kPairs, g, br, bi);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) cmul2(br[jj], bi[jj], lr[jj], li[jj], wr[jj], wi[jj]);
+    };
+    if (single && warp < kConsumerWarps)
+        lane_rope(a.single.query_position, (int64_t)a.single.pos_begin + (int64_t)gsplit * a.chunk);
     allow_dependent_launch();
     grid_dependency_wait();
 
@@ -252,6 +242,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     if (warp == kConsumerWarps) {
         if (lane != 0) return;
         const uint64_t pol = l2_evict_first_policy();
+        // The group's Q rows go first, ahead of the K/V stream.
+        mbar_arrive_expect_tx(qbar, kGroup * kRowBytes);
+        for (int hq = 0; hq < kGroup; ++hq)
+            bulk_load(smem + kOffQ + hq * kRowBytes,
+                      a.q + (int64_t)b * a.q_bstride + (int64_t)(h * kGroup + hq) * a.q_hstride, kRowBytes, qbar, pol);
         int issued = 0;
         bool ok = true;
         for (int t = 0; t < n_tiles; ++t) {
@@ -275,70 +270,38 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         }
         if (!ok) atomicOr(a.ws_status, kDevStatusTimeout);
         // Do not leave while copies into this CTA's shared memory are in flight.
+        mbar_wait(qbar, 0);
         for (int t = max(0, issued - kStages); t < issued; ++t) mbar_wait(&full[t % kStages], (t / kStages) & 1);
         return;
     }
 
     // ======================= consumer warps =======================
-    const int c = warp;
-    const int slot = lane >> 3;  // key within the group of 4 a step handles
-    const int g = lane & 7;      // pairs 8g .. 8g+7 (dims 8g..8g+7 and 64+8g..64+8g+7)
-    const int hh = g >> 1;       // Q head whose score this lane holds after the reduction
     const int qpos = d.query_position;
-
-    // Q rows of the group; the loads are issued before the table work they overlap.
-    uint4 qx[kGroup], qy[kGroup];
-#pragma unroll
-    for (int hq = 0; hq < kGroup; ++hq) {
-        const __nv_bfloat16* qrow = a.q + (int64_t)b * a.q_bstride + (int64_t)(h * kGroup + hq) * a.q_hstride;
-        qx[hq] = *reinterpret_cast<const uint4*>(qrow + 8 * g);
-        qy[hq] = *reinterpret_cast<const uint4*>(qrow + kPairs + 8 * g);
-    }
-
     if (a.mask_out != nullptr && split == 0 && h == 0) {
         const int n_pad = ((d.seq_len + a.kv_block_len - 1) / a.kv_block_len) * a.kv_block_len;
         for (int p = tid; p < n_pad; p += kConsumerThreads)
             a.mask_out[(int64_t)b * a.mask_stride + p] = key_valid(p, d.seq_len, qpos) ? 1 : 0;
     }
-    if (!single) {
-        build_rope_table(steps, rope, qpos, first_pos, tid);
-        named_barrier_sync(1, kConsumerThreads);
-    }
+    if (!single) lane_rope(qpos, first_pos);
 
-    // Q rotated at QUERY_POSITION and pre-scaled by scale*log2(e).
+    // Q rotated at QUERY_POSITION and pre-scaled by scale*log2(e).  Register
+    // slot j of a lane holds Q head j ^ hh, so that the score reduction below
+    // needs no per-lane selects (each lane keeps slots 0/1 and sends 2/3).
     float2 qr[kGroup][4], qi[kGroup][4];
-    {
-        float2 wr[4], wi[4];
-        rope_row8(rope + kRopeQ * kPairs, g, wr, wi);
+    bool ok = mbar_wait(qbar, 0);
 #pragma unroll
-        for (int hq = 0; hq < kGroup; ++hq) {
-            const uint32_t xw[4] = {qx[hq].x, qx[hq].y, qx[hq].z, qx[hq].w};
-            const uint32_t yw[4] = {qy[hq].x, qy[hq].y, qy[hq].z, qy[hq].w};
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                float2 re, im;
-                cmul2(bf16x2_to_float2(xw[jj]), bf16x2_to_float2(yw[jj]), wr[jj], wi[jj], re, im);
-                qr[hq][jj] = __fmul2_rn(re, f2(a.qscale));
-                qi[hq][jj] = __fmul2_rn(im, f2(a.qscale));
-            }
-        }
-    }
-
-    // RoPE factors of this lane's key in step 0 of the current tile
-    // (first key x warp offset x slot offset).
-    float2 wr[4], wi[4], sr[4], si[4], tr[4], ti[4];
-    {
-        float2 br[4], bi[4], cr[4], ci[4], xr[4], xi[4];
-        rope_row8(rope + kRopeStep * kPairs, g, sr, si);
-        rope_row8(rope + kRopeTile * kPairs, g, tr, ti);
-        rope_row8(rope + kRopeBase * kPairs, g, br, bi);
-        rope_row8(rope + (kRopeWarp + c) * kPairs, g, cr, ci);
-        rope_row8(rope + (kRopeSlot + slot) * kPairs, g, xr, xi);
+    for (int j = 0; j < kGroup; ++j) {
+        const uint8_t* qrow = qs + (j ^ hh) * kRowBytes;
+        const uint4 xr = *reinterpret_cast<const uint4*>(qrow + g * 16);
+        const uint4 xi = *reinterpret_cast<const uint4*>(qrow + 128 + g * 16);
+        const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
+        const uint32_t yw[4] = {xi.x, xi.y, xi.z, xi.w};
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
-            float2 tr0, ti0;
-            cmul2(br[jj], bi[jj], cr[jj], ci[jj], tr0, ti0);
-            cmul2(tr0, ti0, xr[jj], xi[jj], wr[jj], wi[jj]);
+            float2 re, im;
+            cmul2(bf16x2_to_float2(xw[jj]), bf16x2_to_float2(yw[jj]), qfr[jj], qfi[jj], re, im);
+            qr[j][jj] = __fmul2_rn(re, f2(a.qscale));
+            qi[j][jj] = __fmul2_rn(im, f2(a.qscale));
         }
     }
 
@@ -392,16 +355,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 }
                 s[hq] = acc.x + acc.y;
             }
-            const bool b2 = lane & 4, b1 = lane & 2;
-            const float t0 = (b2 ? s[2] : s[0]) + __shfl_xor_sync(0xffffffffu, b2 ? s[0] : s[2], 4);
-            const float t1 = (b2 ? s[3] : s[1]) + __shfl_xor_sync(0xffffffffu, b2 ? s[1] : s[3], 4);
-            float u = (b1 ? t1 : t0) + __shfl_xor_sync(0xffffffffu, b1 ? t0 : t1, 2);
+            // Lanes l and l^4 hold the same heads in swapped slot pairs, lanes l
+            // and l^2 in swapped slots: keep 0/1, send 2/3; keep 0, send 1.
+            const float t0 = s[0] + __shfl_xor_sync(0xffffffffu, s[2], 4);
+            const float t1 = s[1] + __shfl_xor_sync(0xffffffffu, s[3], 4);
+            float u = t0 + __shfl_xor_sync(0xffffffffu, t1, 2);
             u += __shfl_xor_sync(0xffffffffu, u, 1);
             sc[step] = r < rows ? u : -INFINITY;
         }
         // Advance the lane's RoPE factors by one tile (exactly every kReanchorTiles).
         if (((t + 1) % kReanchorTiles) == 0) {
-            rope_exact8(steps, g, first_pos + (int64_t)(t + 1) * kTileKeys + c * kKeysPerWarp + slot, wr, wi);
+            rope_exact8(rt, g, first_pos + (int64_t)(t + 1) * kTileKeys + c * kKeysPerWarp + slot, wr, wi);
         } else {
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
@@ -478,8 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 
     // Software pipeline: the P.V of tile t-1 is issued in the same block as
     // the Q.K of tile t, giving each warp two independent instruction streams.
-    bool ok = true;
-    if (n_tiles > 0) {
+    if (ok && n_tiles > 0) {
         if (mbar_wait(&full[0], 0)) {
             float sc[kSteps];
             qk_tile(0, sc);
@@ -585,12 +548,17 @@ __global__ void __launch_bounds__(kHeadDim) split_merge_kernel(const __grid_cons
     const int2 si = m.seqinfo[b];
     const int64_t split_stride = (int64_t)kNumQHeads * kPartialFloats;
     const float* base = m.partials + ((int64_t)si.x * kNumQHeads + qh) * kPartialFloats;
-    // Split s's max and sum (threads s < n_split), block max and weighted sum.
+    // One round trip: split s's (m, l) on thread s, and this thread's acc column
+    // of the first 32 splits, all loaded before any of them is used.
     float ms = -INFINITY, ls = 0.f;
     if (dim < n_split) {
         ms = __ldcg(base + dim * split_stride + 128);
         ls = __ldcg(base + dim * split_stride + 129);
     }
+    constexpr int kBatch = 32;
+    float v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) v[j] = j < n_split ? __ldcg(base + j * split_stride + dim) : 0.f;
     float M = ms;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
@@ -606,15 +574,11 @@ __global__ void __launch_bounds__(kHeadDim) split_merge_kernel(const __grid_cons
     if ((dim & 31) == 0) red[1][dim >> 5] = L;
     __syncthreads();
     L = (red[1][0] + red[1][1]) + (red[1][2] + red[1][3]);
-    float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int s0 = 0; s0 < n_split; s0 += 8) {
-        float v[8];
+    float o4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = s0 + j < n_split ? __ldcg(base + (s0 + j) * split_stride + dim) : 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o8[j] = fmaf(v[j], s0 + j < n_split ? fac[s0 + j] : 0.f, o8[j]);
-    }
-    const float O = ((o8[0] + o8[1]) + (o8[2] + o8[3])) + ((o8[4] + o8[5]) + (o8[6] + o8[7]));
+    for (int j = 0; j < kBatch; ++j) o4[j & 3] = fmaf(v[j], j < n_split ? fac[j] : 0.f, o4[j & 3]);
+    for (int s = kBatch; s < n_split; ++s) o4[s & 3] = fmaf(__ldcg(base + s * split_stride + dim), fac[s], o4[s & 3]);
+    const float O = (o4[0] + o4[1]) + (o4[2] + o4[3]);
     write_result(m.out, b, qh, dim, O, M, L);
 }
 
@@ -682,7 +646,67 @@ cudaError_t launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cud
     return cudaLaunchKernelExC(&cfg, func, args);
 }
 
+// Immutable RoPE tables, one slot per distinct rope_theta (per device).
+__device__ RopeTable g_rope_tables[kRopeTableSlots];
+
 }  // namespace
+
+// Host side of the RoPE table cache.
+namespace {
+struct RopeSlots {
+    bool used[kRopeTableSlots] = {};
+    double theta[kRopeTableSlots] = {};
+};
+std::mutex g_rope_mu;
+RopeSlots g_rope_slots[64];
+
+void build_rope_table_host(double theta, RopeTable& t) {
+    const double two_pi = 2.0 * M_PI;
+    for (int i = 0; i < kPairs; ++i) {
+        const double inv = std::pow(theta, -2.0 * i / (double)kHeadDim);
+        t.step[i] = (uint64_t)std::llround(inv / two_pi * 18446744073709551616.0);  // < 2^62
+        t.rot_step[i] = make_float2((float)std::cos(4.0 * inv), (float)std::sin(4.0 * inv));
+        t.rot_tile[i] = make_float2((float)std::cos(kTileKeys * inv), (float)std::sin(kTileKeys * inv));
+        for (int c = 0; c < kConsumerWarps; ++c)
+            for (int sl = 0; sl < 4; ++sl) {
+                const double ang = (double)(c * kKeysPerWarp + sl) * inv;
+                t.lane_off[c * 4 + sl][i] = make_float2((float)std::cos(ang), (float)std::sin(ang));
+            }
+    }
+}
+}  // namespace
+
+cudaError_t rope_table_for(double theta, const RopeTable** table, bool* out_of_slots) {
+    *out_of_slots = false;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_rope_mu);
+    RopeSlots& rs = g_rope_slots[dev];
+    int slot = -1;
+    for (int i = 0; i < kRopeTableSlots && slot < 0; ++i)
+        if (rs.used[i] && rs.theta[i] == theta) slot = i;
+    void* base = nullptr;
+    e = cudaGetSymbolAddress(&base, g_rope_tables);
+    if (e != cudaSuccess) return e;
+    if (slot < 0) {
+        for (int i = 0; i < kRopeTableSlots && slot < 0; ++i)
+            if (!rs.used[i]) slot = i;
+        if (slot < 0) {
+            *out_of_slots = true;
+            return cudaSuccess;
+        }
+        RopeTable host;
+        build_rope_table_host(theta, host);
+        e = cudaMemcpy(static_cast<RopeTable*>(base) + slot, &host, sizeof(RopeTable), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return e;
+        rs.used[slot] = true;
+        rs.theta[slot] = theta;
+    }
+    *table = static_cast<const RopeTable*>(base) + slot;
+    return cudaSuccess;
+}
 
 int decode_tile_keys() { return kTileKeys; }
 int decode_max_splits() { return kMaxSplitsPerSeq; }

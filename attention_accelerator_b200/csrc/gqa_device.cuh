@@ -55,6 +55,25 @@ __host__ __device__ inline bool key_valid(int64_t p, int seq_len, int query_posi
     return p < seq_len && p <= query_position;
 }
 
+// Decode tiling, shared by the kernel and the host code that builds its tables:
+// 11 consumer warps x 8 keys = one 88-key pipeline tile.
+constexpr int kDecodeConsumerWarps = 11;
+constexpr int kDecodeKeysPerWarp = 8;
+constexpr int kDecodeTileKeys = kDecodeConsumerWarps * kDecodeKeysPerWarp;
+// Lane offsets: a consumer lane's first key sits (8c + s) keys after its CTA's
+// first key (warp c, slot s in 0..3).
+constexpr int kRopeLaneOffsets = kDecodeConsumerWarps * 4;
+
+// Immutable per-(device, rope_theta) RoPE table, computed on the host in double
+// precision and uploaded once.  Pair i turns theta^(-2i/128)/(2*pi) turns per
+// position; `step` holds that as an unsigned Q0.64 fraction.
+struct RopeTable {
+    uint64_t step[kPairs];
+    float2 rot_step[kPairs];                  // e^{i theta_i * 4}: the second group of a warp's keys
+    float2 rot_tile[kPairs];                  // e^{i theta_i * kDecodeTileKeys}: one tile further
+    float2 lane_off[kRopeLaneOffsets][kPairs];  // e^{i theta_i * (8c + s)}, row 4c + s
+};
+
 // Kernel argument block, passed by value as a __grid_constant__ parameter.  The
 // two tensor maps come first: TMA requires them 64-byte aligned in param space.
 struct alignas(64) DecodeArgs {
@@ -81,9 +100,7 @@ struct alignas(64) DecodeArgs {
     uint8_t* mask_out;
     int64_t mask_stride;
     int kv_block_len;
-    uint64_t rope_step[kPairs];  // Q0.64 turns per position for each pair
-    float2 rot_step[kPairs];     // e^{i*theta_i*4}: advance of 4 positions
-    float2 rot_tile[kPairs];     // e^{i*theta_i*TP}: advance of one pipeline tile
+    const RopeTable* rope;  // device copy for this call's rope_theta
 };
 
 // ---------------------------------------------------------------------------

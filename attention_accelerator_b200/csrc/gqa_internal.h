@@ -8,6 +8,13 @@
 namespace gqa {
 
 struct DecodeArgs;
+struct RopeTable;
+
+// Device address of the RoPE table for `theta` on the current device, built and
+// uploaded on first use (a synchronous copy: first use must precede stream
+// capture).  At most kRopeTableSlots distinct thetas per device.
+constexpr int kRopeTableSlots = 4;
+cudaError_t rope_table_for(double theta, const RopeTable** table, bool* out_of_slots);
 
 int decode_tile_keys();
 int decode_max_splits();

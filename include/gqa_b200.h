@@ -50,7 +50,7 @@ enum gqa_status {
     GQA_ERR_CUDA = 13,             /* a CUDA runtime call (launch, attribute, copy) failed */
     GQA_ERR_DEVICE_TIMEOUT = 14,   /* a bounded wait inside a kernel gave up (see gqa_read_status) */
     GQA_ERR_UNSUPPORTED_DEVICE = 15, /* current device is not sm_100 */
-    GQA_ERR_ROPE_THETA = 16        /* rope_theta <= 0 or not finite */
+    GQA_ERR_ROPE_THETA = 16        /* rope_theta <= 0, not finite, or a 5th distinct value on one device */
 };
 
 /* GQA_FLAG_* values for gqa_params.flags. */
@@ -149,6 +149,9 @@ size_t gqa_workspace_bytes(const gqa_params *p, const gqa_seq_desc *descs, int b
  * pyfiles/gen_gqa_wrapper_vectors.py:121-139.
  * q: [32][128] BF16; k, v: the key/value rows (layout from the strides);
  * out: [32][128] BF16 (or gqa_partial_row[32] with GQA_FLAG_PARTIAL_OUT).
+ * The first call on a device with a given rope_theta uploads that theta's
+ * RoPE table (a synchronous copy; make it before any stream capture); up to 4
+ * distinct rope_theta values per device.
  */
 int gqa_decode(const void *q, const void *k, const void *v, void *out,
                const gqa_params *p, void *workspace, size_t workspace_bytes, void *stream);

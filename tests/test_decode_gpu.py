@@ -46,9 +46,18 @@ def run_decode(q_bits, k_bits, v_bits, device, *, layout="position_major", **kw)
 
 
 def assert_parity(golden, got, tight=TIGHT_ULP):
+    """The reference's rule (<= 64 ULP with the 0x3d exemption), then our tighter
+    FP32 bar: <= `tight` ULP wherever the golden is at least 2^-10 of its row's
+    largest magnitude (outputs that nearly cancel carry FP32 rounding of the
+    large terms, a few ULP of a tiny number), and a small mean."""
+    from oracle.bf16 import bf16_to_f32, ulp_distance
     res = check_rows(golden, got, MAX_ULP)
     assert res.passed, res.line()
-    assert res.worst_ulp <= tight, res.line()
+    mag = np.abs(bf16_to_f32(golden))
+    big = mag >= np.ldexp(mag.max(axis=-1, keepdims=True), -10)
+    dist = ulp_distance(golden, got)
+    assert int(dist[big].max(initial=0)) <= tight, res.line()
+    assert res.mean_ulp < 0.1, res.line()
     return res
 
 

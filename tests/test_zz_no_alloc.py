@@ -57,7 +57,7 @@ def test_noalloc_matches_workspace_entry_point(seq_len, cuda_device):
         assert _noalloc(q, k, v, seq_len, got) == _lib.GQA_OK
         torch.cuda.synchronize()
         res = check_rows(torch_to_bits(want), torch_to_bits(got), MAX_ULP)
-        assert res.passed and res.worst_ulp <= TIGHT_ULP, res.line()
+        assert res.passed and res.worst_ulp <= TIGHT_ULP, res.line()  # same kernels: agree to rounding
 
 
 def test_noalloc_rejects_bad_configuration_before_launch(cuda_device):
