@@ -182,6 +182,33 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, seq_len: int | 
     return dev_out
 
 
+@dataclass(frozen=True)
+class SplitPlan:
+    """How a call cuts the keys on the current device (diagnostic)."""
+    splits: int          # key splits in total (each runs on 8 CTAs, one per KV head)
+    keys_per_split: int
+    cluster: int         # > 0: one thread-block cluster per KV head merges on chip
+
+
+def decode_plan(seq_len: int | None = None, *, query_position: int | None = None,
+                plan: "BatchPlan | None" = None) -> SplitPlan:
+    """The split plan of :func:`decode` (``seq_len``) or :func:`decode_batch` (``plan``)."""
+    lib = _lib.load()
+    if (seq_len is None) == (plan is None):
+        raise ValueError("give exactly one of seq_len or plan")
+    splits, keys, cluster = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    if plan is None:
+        p = make_params(seq_len=seq_len, query_position=query_position)
+        st = lib.gqa_decode_plan(ctypes.byref(p), None, 1, ctypes.byref(splits), ctypes.byref(keys),
+                                 ctypes.byref(cluster))
+    else:
+        p = make_params(seq_len=1)
+        st = lib.gqa_decode_plan(ctypes.byref(p), plan.host, plan.batch, ctypes.byref(splits), ctypes.byref(keys),
+                                 ctypes.byref(cluster))
+    _check(st, "decode_plan")
+    return SplitPlan(splits.value, keys.value, cluster.value)
+
+
 @dataclass
 class BatchPlan:
     """Per-sequence register values of a batched call, in host and device memory.

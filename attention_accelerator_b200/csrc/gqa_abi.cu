@@ -18,16 +18,24 @@ static_assert(sizeof(gqa_partial_row) == gqa::kPartialFloats * sizeof(float), "p
 namespace {
 
 constexpr int kMaxDevices = 64;
-constexpr size_t kWsHeaderBytes = 256;
-constexpr int kMinChunk = 64;        // keys: one pipeline tile
+constexpr size_t kWsHeaderBytes = 256;  // status word at 0, per-KV-head arrival counters at 64
+constexpr size_t kWsArrivalsOffset = 64;
+constexpr int kMinChunk = gqa::kDecodeTileKeys;  // keys: one pipeline tile
 constexpr int kMinChunkMultiWave = 256;
 constexpr int kMaxWaves = 16;
 constexpr int kOverheadKeys = 64;    // per-CTA prologue/epilogue cost, in key-equivalents
+// What merging a single sequence's splits adds to its latency, in pipeline
+// tiles of one CTA: the last split's arrival and L2 round trip, or a cluster
+// barrier and distributed-shared-memory round trip.
+constexpr double kLastSplitMergeTiles = 1.5;
+constexpr double kClusterMergeTiles = 0.3;
 
 struct DeviceInfo {
     bool init = false;
     int status = GQA_OK;
     int sms = 0;
+    int cluster_cap[17] = {};  // decode clusters of n CTAs the device holds at once
+    bool cluster_asked[17] = {};  // cluster_cap[n] is known
 };
 
 std::mutex g_mu;
@@ -57,6 +65,19 @@ int current_device(int* sms) {
     if (di.status != GQA_OK) return di.status;
     *sms = di.sms;
     return GQA_OK;
+}
+
+// Decode clusters of n CTAs the current device can hold at once (cached).
+int cluster_capacity(int n) {
+    int dev = 0;
+    if (n < 2 || n > 16 || cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+    std::lock_guard<std::mutex> lock(g_mu);
+    DeviceInfo& di = g_dev[dev];
+    if (!di.cluster_asked[n]) {
+        di.cluster_cap[n] = gqa::decode_cluster_capacity(n);
+        di.cluster_asked[n] = true;
+    }
+    return di.cluster_cap[n];
 }
 
 // cuTensorMapEncodeTiled from the driver, fetched once through the runtime (no -lcuda).
@@ -127,8 +148,8 @@ int check_layout(const void* q, const void* k, const void* v, const void* out, c
         if (p->out_head_stride < gqa::kPartialFloats || p->out_head_stride % 4 || p->out_batch_stride < 0 ||
             p->out_batch_stride % 4)
             return GQA_ERR_ALIGNMENT;
-    } else if (p->out_head_stride < 0 || p->out_batch_stride < 0) {
-        return GQA_ERR_ALIGNMENT;
+    } else if (!stride_ok(p->out_head_stride) || !stride_ok(p->out_batch_stride)) {
+        return GQA_ERR_ALIGNMENT;  // BF16 rows are written 4 elements at a time
     }
     return GQA_OK;
 }
@@ -145,6 +166,7 @@ int check_desc(const gqa::SeqDesc& d, bool need_keys) {
 struct Plan {
     int chunk = 0;
     int total_splits = 0;
+    int cluster = 0;      // > 0: single sequence, splits merged inside thread-block clusters
     int64_t kv_rows = 1;  // tensor-map row extent: one past the last stored row any key uses
     size_t off_seqinfo = 0, off_partials = 0, ws_bytes = 0;
 };
@@ -152,8 +174,12 @@ struct Plan {
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Keys per split: one wave of CTAs for a single sequence; for a batch, the
-// wave count (1..16) that minimises waves x (chunk + per-CTA overhead).
-Plan make_plan(const gqa::SeqDesc* d, int batch, int sms) {
+// wave count (1..16) that minimises waves x (chunk + per-CTA overhead).  A
+// single sequence (allow_cluster) with several splits is instead cut into n
+// <= 16 splits merged inside one cluster per KV head when the device holds all
+// 8 such clusters at once and that costs fewer tiles per CTA than the one-wave
+// plan with its last-split merge.
+Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = false) {
     const int slots = sms / gqa::kNumKVHeads > 0 ? sms / gqa::kNumKVHeads : 1;
     int64_t total = 0, longest = 0;
     for (int b = 0; b < batch; ++b) {
@@ -188,12 +214,38 @@ Plan make_plan(const gqa::SeqDesc* d, int batch, int sms) {
     Plan pl;
     pl.chunk = best_chunk > 0 ? best_chunk : kMinChunk;
     pl.total_splits = (int)splits_for(pl.chunk);
+    if (allow_cluster && batch == 1 && pl.total_splits > 1) {
+        const int tile = gqa::decode_tile_keys();
+        auto tiles = [&](int64_t c) { return (double)((c + tile - 1) / tile); };
+        // One split fewer per KV head when that costs no extra tile: the SMs it
+        // frees take the next call's CTAs while this call's last splits merge.
+        if (slots > 2) {
+            const int c = round8(std::max<int64_t>(kMinChunk, (longest + slots - 2) / (slots - 1)));
+            if (tiles(c) == tiles(pl.chunk)) {
+                pl.chunk = c;
+                pl.total_splits = (int)splits_for(c);
+            }
+        }
+        double best = tiles(pl.chunk) + kLastSplitMergeTiles;
+        for (int n = gqa::decode_max_cluster_splits(); n >= 2; --n) {
+            const int c = round8(std::max<int64_t>(kMinChunk, (longest + n - 1) / n));
+            const int ns = (int)splits_for(c);
+            const double cost = tiles(c) + kClusterMergeTiles;
+            if (ns >= 2 && cost < best && cluster_capacity(ns) >= gqa::kNumKVHeads) {
+                best = cost;
+                pl.chunk = c;
+                pl.total_splits = ns;
+                pl.cluster = ns;
+            }
+        }
+    }
     pl.kv_rows = 1;
     for (int b = 0; b < batch; ++b)
         pl.kv_rows = std::max<int64_t>(pl.kv_rows, d[b].kv_start + gqa::seq_key_count(d[b]));
     pl.off_seqinfo = kWsHeaderBytes;
     pl.off_partials = pl.off_seqinfo + align256((size_t)batch * sizeof(int2));
-    pl.ws_bytes = pl.off_partials + (size_t)pl.total_splits * gqa::kNumKVHeads * gqa::kGroup *
+    const size_t partial_splits = pl.cluster > 0 ? 0 : (size_t)pl.total_splits;  // clusters merge on chip
+    pl.ws_bytes = pl.off_partials + partial_splits * gqa::kNumKVHeads * gqa::kGroup *
                                         gqa::kPartialFloats * sizeof(float);
     return pl;
 }
@@ -320,13 +372,41 @@ size_t gqa_workspace_bytes(const gqa_params* p, const gqa_seq_desc* descs, int b
     if (descs == nullptr) {
         if (batch != 1 || gqa_validate(p) != GQA_OK) return 0;
         const gqa::SeqDesc d = single_desc(p);
-        return make_plan(&d, 1, sms).ws_bytes;
+        return make_plan(&d, 1, sms, true).ws_bytes;
     }
     if (batch < 1) return 0;
     const gqa::SeqDesc* d = reinterpret_cast<const gqa::SeqDesc*>(descs);
     for (int b = 0; b < batch; ++b)
         if (check_desc(d[b], false) != GQA_OK) return 0;
     return make_plan(d, batch, sms).ws_bytes;
+}
+
+int gqa_decode_plan(const gqa_params* p, const gqa_seq_desc* descs, int batch, int* splits, int* keys_per_split,
+                    int* cluster) {
+    if (!p || !splits || !keys_per_split || !cluster) return GQA_ERR_NULL_POINTER;
+    int sms = 0;
+    int st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    Plan pl;
+    if (descs == nullptr) {
+        if (batch != 1) return GQA_ERR_BATCH;
+        st = gqa_validate(p);
+        if (st != GQA_OK) return st;
+        const gqa::SeqDesc d = single_desc(p);
+        pl = make_plan(&d, 1, sms, true);
+    } else {
+        if (batch < 1) return GQA_ERR_BATCH;
+        const gqa::SeqDesc* d = reinterpret_cast<const gqa::SeqDesc*>(descs);
+        for (int b = 0; b < batch; ++b) {
+            st = check_desc(d[b], false);
+            if (st != GQA_OK) return st;
+        }
+        pl = make_plan(d, batch, sms);
+    }
+    *splits = pl.total_splits;
+    *keys_per_split = pl.chunk;
+    *cluster = pl.cluster;
+    return GQA_OK;
 }
 
 int gqa_decode(const void* q, const void* k, const void* v, void* out, const gqa_params* p, void* workspace,
@@ -339,15 +419,17 @@ int gqa_decode(const void* q, const void* k, const void* v, void* out, const gqa
     st = current_device(&sms);
     if (st != GQA_OK) return st;
     const gqa::SeqDesc d = single_desc(p);
-    const Plan pl = make_plan(&d, 1, sms);
+    const Plan pl = make_plan(&d, 1, sms, true);
     if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
     gqa::DecodeArgs a;
     st = fill_args(a, q, k, v, out, p, workspace, pl, 1);
     if (st != GQA_OK) return st;
     a.descs = nullptr;
     a.single = d;
-    if (gqa::launch_decode(a, pl.total_splits * gqa::kNumKVHeads, pl.total_splits, static_cast<cudaStream_t>(stream)) !=
-        cudaSuccess)
+    a.cluster = pl.cluster;
+    if (pl.cluster == 0 && pl.total_splits > 1 && pl.total_splits <= gqa::decode_last_merge_max_splits())
+        a.ws_arrivals = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + kWsArrivalsOffset);
+    if (gqa::launch_decode(a, pl.total_splits, static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return GQA_ERR_CUDA;
     return GQA_OK;
 }
@@ -378,8 +460,7 @@ int gqa_decode_batched(const void* q, const void* k, const void* v, void* out, c
     if (st != GQA_OK) return st;
     a.descs = reinterpret_cast<const gqa::SeqDesc*>(dev_descs);
     a.single = d[0];
-    if (gqa::launch_decode(a, pl.total_splits * gqa::kNumKVHeads, pl.total_splits, static_cast<cudaStream_t>(stream)) !=
-        cudaSuccess)
+    if (gqa::launch_decode(a, pl.total_splits, static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return GQA_ERR_CUDA;
     return GQA_OK;
 }
@@ -454,7 +535,8 @@ int gqa_read_status(void* workspace, void* stream, int* device_status) {
     uint32_t v = 0;
     if (cudaStreamSynchronize(s) != cudaSuccess) return GQA_ERR_CUDA;
     if (cudaMemcpy(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return GQA_ERR_CUDA;
-    if (v != 0 && cudaMemset(workspace, 0, sizeof(v)) != cudaSuccess) return GQA_ERR_CUDA;
+    // After a timed-out wait the arrival counters may be left part-way: clear the header.
+    if (v != 0 && cudaMemset(workspace, 0, kWsHeaderBytes) != cudaSuccess) return GQA_ERR_CUDA;
     *device_status = v ? GQA_ERR_DEVICE_TIMEOUT : GQA_OK;
     return GQA_OK;
 }

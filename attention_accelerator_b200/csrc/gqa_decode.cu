@@ -22,6 +22,12 @@
 //               with one split writes its BF16 rows (O * 1/l,
 //               output_accumulator.v:546-687) directly, otherwise each split
 //               writes an FP32 partial to the workspace for split_merge_kernel.
+//   cluster     (single sequence of up to 16 splits) the splits of one KV head
+//               run as one thread-block cluster: each keeps its partial in
+//               shared memory and, after a cluster barrier, merges 32 of the
+//               head group's 512 outputs from all the cluster's partials over
+//               distributed shared memory -- no second kernel, no workspace
+//               round trip.
 // Both kernels are launched with programmatic dependent launch: everything that
 // reads only the argument block (barrier set-up, RoPE tables) runs before
 // griddepcontrol.wait, overlapping the tail of the previous kernel in the stream.
@@ -128,6 +134,193 @@ __device__ __forceinline__ void write_result(const OutSpec& o, int b, int qh, in
     }
 }
 
+// Four consecutive output elements dim0 .. dim0+3 (dim0 a multiple of 4; rows are 16-byte aligned).
+__device__ __forceinline__ void write_result4(const OutSpec& o, int b, int qh, int dim0, float4 acc, float m,
+                                              float l) {
+    if (o.flags & 1u) {
+        float* r = static_cast<float*>(o.out) + (int64_t)b * o.o_bstride + (int64_t)qh * o.o_hstride;
+        *reinterpret_cast<float4*>(r + dim0) = acc;
+        if (dim0 == 0) *reinterpret_cast<float4*>(r + 128) = make_float4(m, l, 0.f, 0.f);
+    } else {
+        __nv_bfloat16* r = static_cast<__nv_bfloat16*>(o.out) + (int64_t)b * o.o_bstride + (int64_t)qh * o.o_hstride;
+        const __nv_bfloat162 lo = __halves2bfloat162(__float2bfloat16_rn(acc.x / l), __float2bfloat16_rn(acc.y / l));
+        const __nv_bfloat162 hi = __halves2bfloat162(__float2bfloat16_rn(acc.z / l), __float2bfloat16_rn(acc.w / l));
+        uint2 w;
+        w.x = *reinterpret_cast<const uint32_t*>(&lo);
+        w.y = *reinterpret_cast<const uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(r + dim0) = w;
+    }
+}
+
+// Producer (one thread): the group's Q rows, then per tile one TMA box for K
+// and one for V (88 rows of one head, whatever the K/V strides) into the
+// shared-memory ring; returns once its copies have landed.
+__device__ __forceinline__ void produce_tiles(const DecodeArgs& a, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                             uint64_t* qbar, int b, int h, int64_t first_row, int n_tiles) {
+    const uint64_t pol = l2_evict_first_policy();
+    // The group's Q rows go first, ahead of the K/V stream.
+    mbar_arrive_expect_tx(qbar, kGroup * kRowBytes);
+    for (int hq = 0; hq < kGroup; ++hq)
+        bulk_load(smem + kOffQ + hq * kRowBytes,
+                  a.q + (int64_t)b * a.q_bstride + (int64_t)(h * kGroup + hq) * a.q_hstride, kRowBytes, qbar, pol);
+    int issued = 0;
+    bool ok = true;
+    for (int t = 0; t < n_tiles; ++t) {
+        const int st = t % kStages;
+        if (t >= kStages && !mbar_wait(&empty[st], ((t / kStages) - 1) & 1)) {
+            ok = false;
+            break;
+        }
+        uint8_t* kd = smem + st * kStageBytes;
+        uint8_t* vd = kd + kTileBytes;
+        mbar_arrive_expect_tx(&full[st], 2 * kTileBytes);
+        const int row = static_cast<int>(first_row + (int64_t)t * kTileKeys);
+        if (a.kv_rows_inner) {
+            tma_load_3d(kd, &a.kmap, 0, row, h, &full[st], pol);
+            tma_load_3d(vd, &a.vmap, 0, row, h, &full[st], pol);
+        } else {
+            tma_load_3d(kd, &a.kmap, 0, h, row, &full[st], pol);
+            tma_load_3d(vd, &a.vmap, 0, h, row, &full[st], pol);
+        }
+        issued = t + 1;
+    }
+    if (!ok) atomicOr(a.ws_status, kDevStatusTimeout);
+    // Do not leave while copies into this CTA's shared memory are in flight.
+    mbar_wait(qbar, 0);
+    for (int t = max(0, issued - kStages); t < issued; ++t) mbar_wait(&full[t % kStages], (t / kStages) & 1);
+}
+
+// Cluster epilogue of a single sequence: the n splits (CTA ranks 0..n-1) of KV
+// head h each hold their partial (acc[128], m, l per Q head) at `cpart`.  The
+// 512 outputs form 16 groups of 32 (one Q head, 32 dims); group w*n + rank goes
+// to warp w of CTA `rank`, one output per lane, merged as
+//   M = max m_s,  L = sum 2^(m_s - M) l_s,  O = sum 2^(m_s - M) acc_s
+// with split s's (m, l) loaded by lane s.
+constexpr int kMaxClusterSplits = 16;
+static_assert(kConsumerWarps * 2 >= kOutputs / 32, "two splits cover the 16 output groups");
+
+__device__ __forceinline__ void cluster_merge(int n, int rank, int c, int lane, const float* cpart,
+                                              const OutSpec& direct, int h) {
+    cluster_sync_all();  // every split's partial is in its shared memory
+    const int grp = c * n + rank;
+    if (grp < kOutputs / 32) {
+        const int hq = grp >> 2, dim = (grp & 3) * 32 + lane;
+        const float* row = cpart + hq * kPartialFloats;
+        float ms = -INFINITY, ls = 0.f;
+        if (lane < n) {
+            const float2 x = ld_cluster_f32x2(cluster_map(row + 128, lane));
+            ms = x.x;
+            ls = x.y;
+        }
+        float vals[kMaxClusterSplits];
+#pragma unroll
+        for (int s = 0; s < kMaxClusterSplits; ++s) vals[s] = s < n ? ld_cluster_f32(cluster_map(row + dim, s)) : 0.f;
+        float M = ms;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float Mu = M == -INFINITY ? 0.f : M;
+        const float f = lane < n ? exp2f(ms - Mu) : 0.f;
+        float L = ls * f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        float o4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < kMaxClusterSplits; ++s) o4[s & 3] = fmaf(vals[s], __shfl_sync(0xffffffffu, f, s), o4[s & 3]);
+        write_result(direct, 0, h * kGroup + hq, dim, (o4[0] + o4[1]) + (o4[2] + o4[3]), M, L);
+    }
+    cluster_sync_all();  // no CTA leaves while another may still read its partial
+}
+
+// Merge of a single sequence's n <= 32 splits by the last split CTA of KV head
+// h to finish (the others return): each CTA's partial is in the workspace; an
+// arrival counter per KV head (release fence, then atomic add; zeroed again by
+// the last arrival) picks the last one, which reads every split's (m, l) and
+// acc column from L2 in one round trip, then
+//   M = max m_s,  L = sum 2^(m_s - M) l_s,  O = sum 2^(m_s - M) acc_s
+// with warp hq reducing head hq's (m, l) over lanes s.  Consumer thread tid
+// owns outputs tid and tid + kConsumerThreads of the 512.
+constexpr int kLastMergeMaxSplits = 32;
+constexpr int kMergeBatch = 20;  // splits whose acc values a thread loads before the first use
+static_assert(2 * kConsumerThreads >= kOutputs, "two outputs per consumer thread cover the head group");
+static_assert(kConsumerWarps >= kGroup, "one warp per Q head reduces (m, l)");
+
+__device__ __forceinline__ uint32_t arrive_relaxed_gpu(uint32_t* p) {
+    uint32_t old;
+    asm volatile("atom.relaxed.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
+    return old;
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+constexpr int kLastMergeScratchFloats = kGroup * kLastMergeMaxSplits + 2 * kGroup;
+
+__device__ __forceinline__ void last_split_merge(const DecodeArgs& a, int n, int h, int tid, float* sh, int* flag,
+                                                 const OutSpec& direct) {
+    named_barrier_sync(1, kConsumerThreads);  // every partial store of this CTA is issued
+    if (tid == 0) {
+        fence_acq_rel_gpu();  // ... and ordered before the arrival (cumulative through the barrier)
+        const uint32_t prev = arrive_relaxed_gpu(a.ws_arrivals + h);
+        const int last = prev == (uint32_t)(n - 1);
+        if (last) {
+            a.ws_arrivals[h] = 0u;  // the next call's kernel starts after this one completes
+            fence_acq_rel_gpu();    // the other splits' partials are visible to the loads below
+        }
+        *flag = last;
+    }
+    named_barrier_sync(1, kConsumerThreads);
+    if (*flag == 0) return;
+
+    const int warp = tid >> 5, lane = tid & 31;
+    const int64_t sstride = (int64_t)kNumKVHeads * kGroup * kPartialFloats;
+    const float* base = a.ws_partials + (int64_t)h * kGroup * kPartialFloats;
+    float* fsh = sh;                                  // [hq][s]  2^(m_s - M)
+    float* tot = fsh + kGroup * kLastMergeMaxSplits;  // [hq]     (M, L)
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (warp < kGroup && lane < n) ml = __ldcg(reinterpret_cast<const float2*>(base + lane * sstride + warp * kPartialFloats + 128));
+    const int o1 = tid + kConsumerThreads;
+    const bool has1 = o1 < kOutputs;
+    const float* p0 = base + (tid >> 7) * kPartialFloats + (tid & 127);
+    const float* p1 = base + ((has1 ? o1 : 0) >> 7) * kPartialFloats + (o1 & 127);
+    float v0[kMergeBatch], v1[kMergeBatch];
+#pragma unroll
+    for (int j = 0; j < kMergeBatch; ++j) {
+        v0[j] = j < n ? __ldcg(p0 + j * sstride) : 0.f;
+        v1[j] = has1 && j < n ? __ldcg(p1 + j * sstride) : 0.f;
+    }
+    if (warp < kGroup) {
+        float M = ml.x;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float f = lane < n ? exp2f(ml.x - (M == -INFINITY ? 0.f : M)) : 0.f;
+        float L = ml.y * f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        fsh[warp * kLastMergeMaxSplits + lane] = f;
+        if (lane == 0) {
+            tot[2 * warp] = M;
+            tot[2 * warp + 1] = L;
+        }
+    }
+    named_barrier_sync(1, kConsumerThreads);
+    auto finish = [&](int o, const float (&v)[kMergeBatch], const float* p) {
+        const int hq = o >> 7;
+        const float* f = fsh + hq * kLastMergeMaxSplits;
+        float o4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < kMergeBatch; ++j) o4[j & 3] = fmaf(v[j], f[j], o4[j & 3]);  // f[j] = 0 past n
+        float rest = 0.f;
+        for (int s = kMergeBatch; s < n; ++s) rest = fmaf(__ldcg(p + s * sstride), f[s], rest);
+        write_result(direct, 0, h * kGroup + hq, o & 127, ((o4[0] + o4[1]) + (o4[2] + o4[3])) + rest, tot[2 * hq],
+                     tot[2 * hq + 1]);
+    };
+    finish(tid, v0, p0);
+    if (has1) finish(o1, v1, p1);
+}
+
+// Epilogue shared memory (in the drained ring): warp partials, the split's merged
+// partial, the last-split merge's scratch, the warp factors.
+static_assert((kConsumerWarps * kGroup * kPartialFloats + kGroup * kPartialFloats + kLastMergeScratchFloats +
+               2 * kConsumerWarps * kGroup + kGroup) * 4 <= kOffBars, "epilogue buffers fit the ring");
+
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
@@ -141,8 +334,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int tid = threadIdx.x;
-    const int h = blockIdx.x % kNumKVHeads;
-    const int gsplit = blockIdx.x / kNumKVHeads;
+    const bool clustered = a.cluster > 0;  // grid (splits, heads), one cluster per head
+    const int h = clustered ? (int)blockIdx.y : (int)(blockIdx.x % kNumKVHeads);
+    const int gsplit = clustered ? (int)blockIdx.x : (int)(blockIdx.x / kNumKVHeads);
     const bool single = a.descs == nullptr;
 
     uint64_t* qbar = empty + kStages;
@@ -234,44 +428,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const int64_t first_row = d.kv_start + key0;
 
     // The split merge finds each sequence's splits here.
-    if (split == 0 && h == 0 && tid == 0 && n_split > 1) a.ws_seqinfo[b] = make_int2(gsplit, n_split);
+    if (!clustered && split == 0 && h == 0 && tid == 0 && n_split > 1) a.ws_seqinfo[b] = make_int2(gsplit, n_split);
 
     // ======================= producer warp =======================
-    // One elected thread issues, per tile, one TMA box for K and one for V
-    // (64 rows of one head, whatever the K/V strides), then drains its copies.
+    // In a cluster the whole warp also takes part in the epilogue's two cluster
+    // barriers.
     if (warp == kConsumerWarps) {
-        if (lane != 0) return;
-        const uint64_t pol = l2_evict_first_policy();
-        // The group's Q rows go first, ahead of the K/V stream.
-        mbar_arrive_expect_tx(qbar, kGroup * kRowBytes);
-        for (int hq = 0; hq < kGroup; ++hq)
-            bulk_load(smem + kOffQ + hq * kRowBytes,
-                      a.q + (int64_t)b * a.q_bstride + (int64_t)(h * kGroup + hq) * a.q_hstride, kRowBytes, qbar, pol);
-        int issued = 0;
-        bool ok = true;
-        for (int t = 0; t < n_tiles; ++t) {
-            const int st = t % kStages;
-            if (t >= kStages && !mbar_wait(&empty[st], ((t / kStages) - 1) & 1)) {
-                ok = false;
-                break;
-            }
-            uint8_t* kd = smem + st * kStageBytes;
-            uint8_t* vd = kd + kTileBytes;
-            mbar_arrive_expect_tx(&full[st], 2 * kTileBytes);
-            const int row = static_cast<int>(first_row + (int64_t)t * kTileKeys);
-            if (a.kv_rows_inner) {
-                tma_load_3d(kd, &a.kmap, 0, row, h, &full[st], pol);
-                tma_load_3d(vd, &a.vmap, 0, row, h, &full[st], pol);
-            } else {
-                tma_load_3d(kd, &a.kmap, 0, h, row, &full[st], pol);
-                tma_load_3d(vd, &a.vmap, 0, h, row, &full[st], pol);
-            }
-            issued = t + 1;
+        if (lane == 0) produce_tiles(a, smem, full, empty, qbar, b, h, first_row, n_tiles);
+        if (clustered) {
+            __syncwarp();
+            cluster_sync_all();  // partials published
+            cluster_sync_all();  // partials read: shared memory may be released
         }
-        if (!ok) atomicOr(a.ws_status, kDevStatusTimeout);
-        // Do not leave while copies into this CTA's shared memory are in flight.
-        mbar_wait(qbar, 0);
-        for (int t = max(0, issued - kStages); t < issued; ++t) mbar_wait(&full[t % kStages], (t / kStages) & 1);
         return;
     }
 
@@ -490,35 +658,55 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     named_barrier_sync(1, kConsumerThreads);
 
     const OutSpec direct{a.out, a.o_bstride, a.o_hstride, a.flags};
-    float* part = a.ws_partials + ((int64_t)gsplit * kNumKVHeads + h) * kGroup * kPartialFloats;
-    for (int o = tid; o < kOutputs; o += kConsumerThreads) {
-        const int hq = o >> 7, dim = o & 127;
-        float mw[kConsumerWarps];
+    // Shared memory behind the warp partials: the split's merged partial (for a
+    // cluster), the last-split merge's scratch, and the warp factors.
+    float* cpart = cb + kConsumerWarps * kGroup * kPartialFloats;
+    float* lsm = cpart + kGroup * kPartialFloats;
+    float* wf = lsm + kLastMergeScratchFloats;  // [w][hq]  2^(m_w - M)
+    float* wl = wf + kConsumerWarps * kGroup;   // [w][hq]  l_w * 2^(m_w - M)
+    float* wm = wl + kConsumerWarps * kGroup;   // [hq]     M
+    // Factors once per (warp, head): thread t < 44 owns warp t / 4, head t % 4.
+    if (tid < kConsumerWarps * kGroup) {
+        const int hq = tid & 3;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-            mw[w] = cb[(w * kGroup + hq) * kPartialFloats + 128];
-            M = fmaxf(M, mw[w]);
-        }
-        const float Mu = M == -INFINITY ? 0.f : M;
-        float L = 0.f, O = 0.f;
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cb[(w * kGroup + hq) * kPartialFloats + 128]);
+        const float* row = cb + tid * kPartialFloats;  // warp tid / 4, head tid % 4
+        const float f = exp2f(row[128] - (M == -INFINITY ? 0.f : M));
+        wf[tid] = f;
+        wl[tid] = row[129] * f;
+        if (tid < kGroup) wm[hq] = M;
+    }
+    named_barrier_sync(1, kConsumerThreads);
+    // Thread t < 128 merges head t / 32, dims 4 (t % 32) .. +3.
+    float* part = clustered ? cpart : a.ws_partials + ((int64_t)gsplit * kNumKVHeads + h) * kGroup * kPartialFloats;
+    if (tid < kOutputs / 4) {
+        const int hq = tid >> 5, d0 = (tid & 31) * 4;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        float L = 0.f;
 #pragma unroll
         for (int w = 0; w < kConsumerWarps; ++w) {
-            const float* row = cb + (w * kGroup + hq) * kPartialFloats;
-            const float f = exp2f(mw[w] - Mu);
-            L = fmaf(row[129], f, L);
-            O = fmaf(row[dim], f, O);
+            const float f = wf[w * kGroup + hq];
+            const float4 x = *reinterpret_cast<const float4*>(cb + (w * kGroup + hq) * kPartialFloats + d0);
+            O = make_float4(fmaf(x.x, f, O.x), fmaf(x.y, f, O.y), fmaf(x.z, f, O.z), fmaf(x.w, f, O.w));
+            L += wl[w * kGroup + hq];
         }
-        if (n_split == 1) {
-            write_result(direct, b, h * kGroup + hq, dim, O, M, L);
+        const float M = wm[hq];
+        if (n_split == 1 && !clustered) {
+            write_result4(direct, b, h * kGroup + hq, d0, O, M, L);
         } else {
             float* row = part + hq * kPartialFloats;
-            row[dim] = O;
-            if (dim == 0) {
+            *reinterpret_cast<float4*>(row + d0) = O;
+            if (d0 == 0) {
                 row[128] = M;
                 row[129] = L;
             }
         }
+    }
+    if (clustered) {
+        cluster_merge(a.cluster, gsplit, c, lane, cpart, direct, h);
+    } else if (a.ws_arrivals != nullptr && n_split > 1) {
+        last_split_merge(a, n_split, h, tid, lsm, info + 2, direct);
     }
 }
 
@@ -632,17 +820,27 @@ __global__ void __launch_bounds__(256) rope_rows_kernel(const __nv_bfloat16* __r
     }
 }
 
-cudaError_t launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args) {
+// Launch with programmatic dependent launch and, for cluster_x > 0, thread-block
+// clusters of (cluster_x, 1, 1).
+cudaError_t launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args,
+                       int cluster_x = 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (cluster_x > 0) {
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = cluster_x;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        cfg.numAttrs = 2;
+    }
     return cudaLaunchKernelExC(&cfg, func, args);
 }
 
@@ -712,16 +910,49 @@ int decode_tile_keys() { return kTileKeys; }
 int decode_max_splits() { return kMaxSplitsPerSeq; }
 size_t decode_smem_bytes() { return kSmemBytes; }
 
+int decode_max_cluster_splits() { return kMaxClusterSplits; }
+int decode_last_merge_max_splits() { return kLastMergeMaxSplits; }
+
 cudaError_t decode_prepare(int device) {
     (void)device;
-    return cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    // Clusters of up to 16 CTAs (above 8 is opt-in); without it clusters stay off.
+    if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        (void)cudaGetLastError();
+    return cudaSuccess;
 }
 
-cudaError_t launch_decode(const DecodeArgs& a, int grid, int total_splits, cudaStream_t stream) {
+int decode_cluster_capacity(int cluster) {
+    if (cluster < 2 || cluster > kMaxClusterSplits) return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cluster, kNumKVHeads);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, decode_kernel, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+cudaError_t launch_decode(const DecodeArgs& a, int total_splits, cudaStream_t stream) {
     void* dargs[] = {const_cast<DecodeArgs*>(&a)};
-    cudaError_t e = launch_pdl(reinterpret_cast<const void*>(decode_kernel), dim3(grid), dim3(kThreads), kSmemBytes,
-                               stream, dargs);
-    if (e != cudaSuccess || total_splits <= a.batch) return e;  // every sequence had one split
+    if (a.cluster > 0)  // single sequence, merged inside the clusters
+        return launch_pdl(reinterpret_cast<const void*>(decode_kernel), dim3(a.cluster, kNumKVHeads), dim3(kThreads),
+                          kSmemBytes, stream, dargs, a.cluster);
+    cudaError_t e = launch_pdl(reinterpret_cast<const void*>(decode_kernel), dim3(total_splits * kNumKVHeads),
+                               dim3(kThreads), kSmemBytes, stream, dargs);
+    // Done when every sequence had one split or the last split of each head merged.
+    if (e != cudaSuccess || total_splits <= a.batch || a.ws_arrivals != nullptr) return e;
     MergeArgs m;
     m.partials = a.ws_partials;
     m.seqinfo = a.ws_seqinfo;

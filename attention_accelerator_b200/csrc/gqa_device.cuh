@@ -101,6 +101,10 @@ struct alignas(64) DecodeArgs {
     int64_t mask_stride;
     int kv_block_len;
     const RopeTable* rope;  // device copy for this call's rope_theta
+    int cluster;            // > 0: single sequence, grid (cluster, 8), the splits of a KV head form one
+                            // thread-block cluster and merge through distributed shared memory
+    uint32_t* ws_arrivals;  // non-null: single sequence, the last split of each KV head to finish merges
+                            // (one arrival counter per KV head, zero between calls)
 };
 
 // ---------------------------------------------------------------------------
@@ -187,6 +191,30 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Thread-block cluster barrier (release on arrive, acquire on wait) and loads
+// from another CTA's shared memory in the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_map(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ float2 ld_cluster_f32x2(uint32_t addr) {
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+    return v;
 }
 
 __device__ __forceinline__ uint4 lds128(const void* p) {

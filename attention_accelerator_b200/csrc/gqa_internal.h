@@ -20,7 +20,16 @@ int decode_tile_keys();
 int decode_max_splits();
 size_t decode_smem_bytes();
 cudaError_t decode_prepare(int device);
-cudaError_t launch_decode(const DecodeArgs& a, int grid, int total_splits, cudaStream_t stream);
+// Most splits of one sequence the in-cluster merge takes, and how many clusters
+// of `cluster` decode CTAs the current device can hold at once (0: none).
+int decode_max_cluster_splits();
+// Most splits of one sequence the last-split merge takes (more: split_merge_kernel).
+int decode_last_merge_max_splits();
+int decode_cluster_capacity(int cluster);
+// Decode of a.batch sequences in total_splits splits (grid total_splits x 8 CTAs,
+// then split_merge_kernel when a sequence has several splits), or, for
+// a.cluster > 0, one sequence in a.cluster splits merged inside the clusters.
+cudaError_t launch_decode(const DecodeArgs& a, int total_splits, cudaStream_t stream);
 cudaError_t launch_combine(const float* parts, int n_parts, int64_t part_stride, int64_t batch_stride, int batch,
                            void* out, int64_t o_bstride, int64_t o_hstride, cudaStream_t stream);
 cudaError_t launch_rope_rows(const void* x, const int32_t* pos, float* out, int rows, const uint64_t* step,

@@ -163,8 +163,12 @@ class SingleDecode(Workload):
 
     def config(self):
         lay = "position_major [S,8,128]" if self.layout == "position_major" else "head_major [8,S,128]"
+        sp = self.gqa.decode_plan(self.S, query_position=self.qpos)
+        merge = (f"in-cluster merge, clusters of {sp.cluster}" if sp.cluster else
+                 "last-split merge" if sp.splits > 1 else "none")
         return {"workload": self.name, "batch_per_gpu": 1, "seq_len": self.S, "query_position": self.qpos,
-                "kv_block_len": 16, "kv_layout": f"{lay} bf16", "l2": self.l2_note}
+                "kv_block_len": 16, "kv_layout": f"{lay} bf16", "l2": self.l2_note,
+                "splits": f"{sp.splits} x {sp.keys_per_split} keys x 8 KV heads ({merge})"}
 
     def e2e_inputs(self):
         t = self.torch

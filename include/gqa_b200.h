@@ -136,11 +136,26 @@ int gqa_validate(const gqa_params *p);
  * Bytes of device workspace a call needs (0 on invalid input).  `descs` is the
  * host copy of the batch's descriptors, or NULL with batch == 1 for a
  * single-sequence call described by p->seq_len / p->query_position.
- * The workspace's first 4 bytes (the device status word) must be zero when it
- * is allocated; the rest needs no initialisation (every call writes its split
- * partials before reading them).
+ * The workspace's first 256 bytes (the device status word and the per-KV-head
+ * arrival counters of the single-sequence split merge) must be zero when it is
+ * allocated; every call leaves the counters zero again, and gqa_read_status
+ * clears the whole header after a timed-out wait.  The rest needs no
+ * initialisation (every call writes its split partials before reading them).
+ * Calls that share a workspace must be ordered (one stream).
  */
 size_t gqa_workspace_bytes(const gqa_params *p, const gqa_seq_desc *descs, int batch);
+
+/*
+ * Diagnostic (no reference counterpart): how a call on the current device cuts
+ * the keys.  `descs`/`batch` as for gqa_workspace_bytes.  Writes the total
+ * number of key splits, the keys per split, and the cluster size (> 0 when a
+ * single sequence's splits of each KV head run as one thread-block cluster and
+ * merge on chip; 0 when the last split of each KV head to finish merges them
+ * (single sequence) or split_merge_kernel does (batched call)).  Returns a
+ * status.
+ */
+int gqa_decode_plan(const gqa_params *p, const gqa_seq_desc *descs, int batch, int *splits, int *keys_per_split,
+                    int *cluster);
 
 /*
  * Single-token decode of one sequence: the operation the reference performs

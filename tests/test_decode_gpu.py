@@ -285,3 +285,58 @@ def test_long_context_131072(cuda_device):
                                       vd[r * step:(r + 1) * step], plan))
     split = torch_to_bits(gqa.combine_partials(torch.stack(parts)))[0]
     assert check_rows(got, split, 2).passed  # summation order differs; both match the oracle above
+
+
+def test_split_plans(cuda_device):
+    """Short single sequences merge their splits inside clusters (one per KV head);
+    longer ones in the last split of each KV head to finish; batches in
+    split_merge_kernel."""
+    assert gqa.decode_plan(30) == gqa.SplitPlan(1, 88, 0)
+    p = gqa.decode_plan(600)
+    assert 2 <= p.cluster <= 16 and p.splits == p.cluster and p.splits * p.keys_per_split >= 600
+    for s in (4096, 131072):
+        p = gqa.decode_plan(s)
+        assert p.cluster == 0 and p.splits > 1 and p.splits * p.keys_per_split >= s
+    batch = gqa.decode_plan(plan=gqa.plan_batch([4096], device=cuda_device))
+    assert batch.cluster == 0 and batch.splits > 1
+
+
+# (seq_len, qpos): 100 / 600 / 1000 keys take the cluster merge, the rest the
+# last-split merge.
+@pytest.mark.parametrize("seq_len,qpos", [(100, 99), (600, 599), (1000, 999), (4096, 4095), (4096, 1500),
+                                          (20000, 19999), (33000, 32999)])
+def test_single_sequence_merges_match_split_merge_kernel(seq_len, qpos, cuda_device):
+    """The single-sequence merges (cluster or last split) and split_merge_kernel
+    (a batch of one) agree to FP32 rounding, and both meet the oracle."""
+    assert gqa.decode_plan(seq_len, query_position=qpos).splits > 1
+    q, k, v = normal_inputs(seq_len, seed=seq_len + qpos)
+    clustered = run_decode(q, k, v, cuda_device, seq_len=seq_len, query_position=qpos)
+    plan = gqa.plan_batch([seq_len], query_positions=[qpos], device=cuda_device)
+    assert gqa.decode_plan(plan=plan).cluster == 0
+    merged = torch_to_bits(gqa.decode_batch(bits_to_torch(q[None], cuda_device),
+                                            bits_to_torch(k.transpose(1, 0, 2).copy(), cuda_device),
+                                            bits_to_torch(v.transpose(1, 0, 2).copy(), cuda_device), plan))[0]
+    assert check_rows(merged, clustered, 2).passed
+    golden = gqa_golden(q, k, v, seq_len, qpos, exact=seq_len <= 1024)
+    assert_parity(golden, clustered)
+    assert_parity(golden, merged)
+
+
+def test_interleaved_split_counts_share_workspace(cuda_device):
+    """Calls with different split counts and merges on one stream (one workspace):
+    the per-head arrival counters return to zero after every call, so each
+    result repeats bit for bit."""
+    lens = [4096, 20000, 600, 2000, 131, 4096]
+    inputs = {s: normal_inputs(s, seed=s) for s in set(lens)}
+    first = {}
+    for rnd in range(3):
+        for s in lens:
+            got = run_decode(*inputs[s], cuda_device, seq_len=s, query_position=s - 1)
+            if s in first:
+                np.testing.assert_array_equal(first[s], got)
+            else:
+                first[s] = got
+    from attention_accelerator_b200 import api
+    torch.cuda.synchronize()
+    ws = api._workspace(cuda_device, api._stream_ptr(cuda_device), 4096)
+    assert int(torch.count_nonzero(ws[:256])) == 0  # status word and arrival counters
