@@ -62,6 +62,17 @@ class GqaSeqDesc(ctypes.Structure):
                 ("pos_end", ctypes.c_int32)]
 
 
+class GqaChunkParams(ctypes.Structure):
+    """Mirror of ``struct gqa_chunk_params`` (48 bytes)."""
+    _fields_ = [("batch", ctypes.c_uint32), ("n_queries", ctypes.c_uint32),
+                ("first_position", ctypes.c_uint32), ("reserved", ctypes.c_uint32),
+                ("q_query_stride", ctypes.c_int64), ("out_query_stride", ctypes.c_int64),
+                ("k_batch_stride", ctypes.c_int64), ("v_batch_stride", ctypes.c_int64)]
+
+
+CHUNKED_WORKSPACE_BYTES = 256
+CHUNKED_MAX_QUERIES = 128
+
 _P = ctypes.c_void_p
 _SIGNATURES = {
     "gqa_status_string": (ctypes.c_char_p, [ctypes.c_int]),
@@ -76,6 +87,8 @@ _SIGNATURES = {
     "gqa_decode_noalloc": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), _P]),
     "gqa_decode_batched": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), ctypes.POINTER(GqaSeqDesc),
                                           _P, ctypes.c_int, _P, ctypes.c_size_t, _P]),
+    "gqa_decode_chunked": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), ctypes.POINTER(GqaChunkParams),
+                                          _P, ctypes.c_size_t, _P]),
     "gqa_combine_partials": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _P,
                                             ctypes.c_int64, ctypes.c_int64, _P]),
     "gqa_rope_rows": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_float, _P]),

@@ -182,6 +182,51 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, seq_len: int | 
     return dev_out
 
 
+def decode_chunked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, first_position: int,
+                   seq_len: int | None = None, kv_block_len: int = DEFAULT_KV_BLOCK_LEN,
+                   scale: float | None = None, layout: str = "position_major", rope_theta: float = ROPE_THETA,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Chunked multi-query decode on the tensor cores.
+
+    ``q``: BF16 ``[B, n, 32, 128]`` with n <= 128; query i of sequence b sits at
+    position ``first_position + i`` and is answered exactly as :func:`decode`
+    with that ``query_position`` and ``seq_len`` (keys p < SEQ_LEN, p <= position).
+    ``k``/``v``: BF16 ``[B, rows, 8, 128]`` (``"position_major"``) or
+    ``[B, 8, rows, 128]`` (``"head_major"``), rows >= SEQ_LEN.  Returns BF16
+    ``[B, n, 32, 128]``.
+    """
+    lib = _lib.load()
+    if q.dim() != 4 or tuple(q.shape[-2:]) != (N_Q_HEADS, HEAD_DIM) or q.dtype != torch.bfloat16 or q.stride(-1) != 1:
+        raise ValueError("q must be bfloat16 [B, n, 32, 128] with a contiguous last dim")
+    batch, n = q.shape[0], q.shape[1]
+    if k.dim() != 4 or v.dim() != 4 or k.shape[0] != batch or v.shape[0] != batch:
+        raise ValueError("k and v must be [B, rows, 8, 128] or [B, 8, rows, 128]")
+    rows_dim = 1 if layout == "position_major" else 2
+    if seq_len is None:
+        seq_len = k.shape[rows_dim]
+    p = make_params(seq_len=seq_len, query_position=first_position + n - 1, kv_block_len=kv_block_len, scale=scale,
+                    rope_theta=rope_theta)
+    for t in (k, v):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.shape[rows_dim] < seq_len:
+            raise ValueError(f"K/V must be bfloat16 with >= SEQ_LEN={seq_len} rows and a contiguous last dim")
+    head_dim_idx = 2 if layout == "position_major" else 1
+    p.k_pos_stride, p.k_head_stride = k.stride(rows_dim), k.stride(head_dim_idx)
+    p.v_pos_stride, p.v_head_stride = v.stride(rows_dim), v.stride(head_dim_idx)
+    device = q.device
+    if out is None:
+        out = torch.empty((batch, n, N_Q_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=device)
+    p.q_batch_stride, p.q_head_stride = q.stride(0), q.stride(2)
+    p.out_batch_stride, p.out_head_stride = out.stride(0), out.stride(2)
+    c = _lib.GqaChunkParams(batch=batch, n_queries=n, first_position=first_position, reserved=0,
+                            q_query_stride=q.stride(1), out_query_stride=out.stride(1),
+                            k_batch_stride=k.stride(0), v_batch_stride=v.stride(0))
+    stream = _stream_ptr(device)
+    ws = _workspace(device, stream, _lib.CHUNKED_WORKSPACE_BYTES)
+    _check(lib.gqa_decode_chunked(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), ctypes.byref(p),
+                                  ctypes.byref(c), ws.data_ptr(), ws.numel(), stream), "decode_chunked")
+    return out
+
+
 @dataclass(frozen=True)
 class SplitPlan:
     """How a call cuts the keys on the current device (diagnostic)."""

@@ -56,7 +56,7 @@ int current_device(int* sms) {
         }
         if (major != 10 || minor != 0) {
             di.status = GQA_ERR_UNSUPPORTED_DEVICE;
-        } else if (gqa::decode_prepare(dev) != cudaSuccess) {
+        } else if (gqa::decode_prepare(dev) != cudaSuccess || gqa::chunked_prepare() != cudaSuccess) {
             di.status = GQA_ERR_CUDA;
         }
         di.sms = n;
@@ -119,6 +119,39 @@ int make_kv_map(CUtensorMap* map, const void* base, int64_t pos_stride, int64_t 
     }
     const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? GQA_OK : GQA_ERR_ALIGNMENT;
+}
+
+// 4-D tensor map over a batch of K or V caches for the chunked kernel:
+// (head_dim, head, row, batch) for position-major rows or (head_dim, row, head,
+// batch) for head-major; box = 64 dims x 64 rows of one head, 128-byte swizzle
+// (the tensor cores' K-major / MN-major operand layout).  Rows past `rows` read
+// as zeros.
+int make_kv_map_batched(CUtensorMap* map, const void* base, int64_t pos_stride, int64_t head_stride,
+                        int64_t batch_stride, int64_t rows, int64_t batch, int* rows_inner) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+    if (!encode) return GQA_ERR_CUDA;
+    const cuuint32_t tile = (cuuint32_t)gqa::chunked_tile_keys();
+    cuuint64_t dims[4];
+    cuuint64_t strides[3];
+    cuuint32_t box[4];
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (batch > 1 && batch_stride <= 0) return GQA_ERR_ALIGNMENT;
+    const cuuint64_t bstride = (cuuint64_t)(batch_stride > 0 ? batch_stride : rows * (pos_stride > head_stride ? pos_stride : head_stride)) * 2;
+    if (pos_stride <= head_stride) {
+        dims[0] = gqa::kHeadDim; dims[1] = (cuuint64_t)rows; dims[2] = gqa::kNumKVHeads; dims[3] = (cuuint64_t)batch;
+        strides[0] = (cuuint64_t)pos_stride * 2; strides[1] = (cuuint64_t)head_stride * 2; strides[2] = bstride;
+        box[0] = 64; box[1] = tile; box[2] = 1; box[3] = 1;
+        *rows_inner = 1;
+    } else {
+        dims[0] = gqa::kHeadDim; dims[1] = gqa::kNumKVHeads; dims[2] = (cuuint64_t)rows; dims[3] = (cuuint64_t)batch;
+        strides[0] = (cuuint64_t)head_stride * 2; strides[1] = (cuuint64_t)pos_stride * 2; strides[2] = bstride;
+        box[0] = 64; box[1] = 1; box[2] = tile; box[3] = 1;
+        *rows_inner = 0;
+    }
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+                              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? GQA_OK : GQA_ERR_ALIGNMENT;
 }
@@ -476,6 +509,59 @@ int gqa_combine_partials(const float* partials, int n_parts, int64_t part_stride
     if (gqa::launch_combine(partials, n_parts, part_stride, batch_stride, batch, out, out_batch_stride,
                             out_head_stride, static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return GQA_ERR_CUDA;
+    return GQA_OK;
+}
+
+int gqa_decode_chunked(const void* q, const void* k, const void* v, void* out, const gqa_params* p,
+                       const gqa_chunk_params* c, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!p || !c) return GQA_ERR_NULL_POINTER;
+    if (c->batch < 1 || c->batch > 65535u || c->n_queries < 1 || c->n_queries > (uint32_t)gqa::chunked_max_queries() ||
+        c->reserved != 0)
+        return GQA_ERR_BATCH;
+    if ((uint64_t)c->first_position + c->n_queries > p->seq_len) return GQA_ERR_QUERY_POSITION;
+    gqa_params last = *p;
+    last.query_position = c->first_position + c->n_queries - 1;
+    int st = gqa_validate(&last);
+    if (st != GQA_OK) return st;
+    if (p->flags != 0 || p->mask_out != nullptr) return GQA_ERR_BATCH;
+    st = check_layout(q, k, v, out, p);
+    if (st != GQA_OK) return st;
+    if (!stride_ok(c->q_query_stride) || !stride_ok(c->out_query_stride) || !stride_ok(c->k_batch_stride) ||
+        !stride_ok(c->v_batch_stride))
+        return GQA_ERR_ALIGNMENT;
+    if (!workspace || !aligned16(workspace) || workspace_bytes < GQA_CHUNKED_WORKSPACE_BYTES) return GQA_ERR_WORKSPACE;
+    int sms = 0;
+    st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    gqa::ChunkLaunch l;
+    std::memset(&l, 0, sizeof(l));
+    int inner_k = 0, inner_v = 0;
+    st = make_kv_map_batched(&l.kmap, k, p->k_pos_stride, p->k_head_stride, c->k_batch_stride, p->seq_len, c->batch,
+                             &inner_k);
+    if (st != GQA_OK) return st;
+    st = make_kv_map_batched(&l.vmap, v, p->v_pos_stride, p->v_head_stride, c->v_batch_stride, p->seq_len, c->batch,
+                             &inner_v);
+    if (st != GQA_OK) return st;
+    if (inner_k != inner_v) return GQA_ERR_ALIGNMENT;
+    l.kv_rows_inner = inner_k;
+    l.q = q;
+    l.out = out;
+    l.q_bstride = p->q_batch_stride;
+    l.q_istride = c->q_query_stride;
+    l.q_hstride = p->q_head_stride;
+    l.o_bstride = p->out_batch_stride;
+    l.o_istride = c->out_query_stride;
+    l.o_hstride = p->out_head_stride;
+    l.batch = (int)c->batch;
+    l.seq_len = (int)p->seq_len;
+    l.first_pos = (int)c->first_position;
+    l.n_queries = (int)c->n_queries;
+    l.qscale = (float)((double)p->scale * 1.4426950408889634);
+    l.status = static_cast<uint32_t*>(workspace);
+    bool out_of_slots = false;
+    if (gqa::rope_table_for((double)p->rope_theta, &l.rope, &out_of_slots) != cudaSuccess) return GQA_ERR_CUDA;
+    if (out_of_slots) return GQA_ERR_ROPE_THETA;
+    if (gqa::launch_chunked(l, static_cast<cudaStream_t>(stream)) != cudaSuccess) return GQA_ERR_CUDA;
     return GQA_OK;
 }
 

@@ -1,0 +1,638 @@
+// gqa_chunked.cu -- chunked multi-query GQA decode on the fifth-generation
+// tensor cores (tcgen05.mma with TMEM accumulators), sm_100a.
+//
+// A chunk is up to 128 consecutive query positions t0 .. t0+n-1 of one
+// sequence; query i is answered exactly as one single-position call of the
+// reference with QUERY_POSITION = t0 + i (gen_gqa_wrapper_vectors.py:121-139):
+// RoPE of Q at its position and of every K row at its own, scores scaled by
+// 1/sqrt(128) over keys p < SEQ_LEN and p <= t, softmax, weighted V, BF16 RNE.
+// With 128 queries per KV head group the work is a dense contraction
+// (S = Q K^T, O = P V), so it runs on the tensor cores.
+//
+// Precision.  The reference rule is <= 64 BF16 ULP against a float64 golden
+// with no relative floor: outputs that nearly cancel make it as strict as FP32
+// arithmetic.  One BF16 product per operand pair misses it on ~0.5% of the
+// outputs, so every operand is split into three BF16 parts carrying 24
+// significant bits (x = x_h + x_m + x_l), and the products whose size is at
+// least 2^-24 of the leading one are accumulated in FP32 by the tensor core:
+//   S = sum over (i, j) in {(l,h), (m,m), (h,l), (m,h), (h,m), (h,h)} of Q_i K_j^T
+//   O = sum over i in {l, m, h} of P_i V                    (V is exact in BF16)
+// i.e. nine BF16 MMAs where plain BF16 attention issues two.  The tensor-core
+// accumulator is only trusted over short chains: each 64-key tile's P V goes to
+// a fresh TMEM accumulator (12 MMAs), and the softmax threads fold it into the
+// running output with correctly rounded FP32 FMAs (O = O * 2^(m_old - m_new) +
+// O_tile), which also makes the online-softmax rescale exact and free.
+//
+// One CTA per (sequence, Q head): M = 128 query rows (TMEM lanes).
+//   warps 0-3   softmax: thread r owns query row r.  Prologue: Q row r rotated
+//               at its position, scaled by scale*log2(e), split, stored to TMEM
+//               (A operand of S).  Per 64-key tile: S row from TMEM, mask, online
+//               softmax, P split into shared memory (A operand of O_tile), and
+//               the previous tile's O_tile folded into the running O in TMEM.
+//               Epilogue: O / l -> BF16 row.
+//   warps 4-7   K rotation: each 64-key K tile lands (TMA, 128-byte swizzle) in
+//               the part-h buffer; the warps rotate it at the key positions and
+//               write the three parts in place / beside it (B operand of S).
+//   warp 8      TMA producer (2-stage ring of K tiles, 3-stage ring of V tiles)
+//               and TMEM allocator.
+//   warp 9      MMA issuer (one thread): S(j+1) is issued as soon as the
+//               softmax has read S(j), so it overlaps softmax(j); O_tile(j) =
+//               P(j) V(j) follows when P(j) is in shared memory.
+#include "gqa_device.cuh"
+#include "gqa_internal.h"
+
+#include <cmath>
+#include <cstring>
+
+namespace gqa {
+
+namespace {
+
+constexpr int kRows = 128;                       // query rows per CTA
+constexpr int kTile = 64;                        // keys per pipeline tile
+constexpr int kKStages = 2;                      // K ring (three parts per stage)
+constexpr int kVStages = 3;                      // V ring
+constexpr int kBlockBytes = kTile * 128;         // 64 rows x 64 BF16: one 128-byte swizzle span per row
+constexpr int kPartBytes = 2 * kBlockBytes;      // a K part or a V tile: dims 0-63 block, dims 64-127 block
+constexpr int kKStageBytes = 3 * kPartBytes;     // K_h, K_m, K_l
+constexpr int kPPartBytes = kRows * 128;         // one P part: 128 rows x 64 keys BF16
+constexpr int kSoftmaxWarps = 4;
+constexpr int kRotWarps = 4;
+constexpr int kProducerWarp = kSoftmaxWarps + kRotWarps;  // 8
+constexpr int kMmaWarp = kProducerWarp + 1;               // 9
+constexpr int kThreads = (kMmaWarp + 1) * 32;             // 320
+constexpr int kRotThreads = kRotWarps * 32;
+constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+
+// TMEM columns (32-bit, 128 lanes): running O, the tile accumulator O_tile,
+// the S accumulator, and the Q parts (A operand: 128 dims = 64 columns of BF16
+// pairs each).
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 0;
+constexpr uint32_t kColOT = 128;
+constexpr uint32_t kColS = 256;
+constexpr uint32_t kColQ = 320;
+static_assert(kColQ + 3 * 64 <= kTmemCols, "TMEM budget");
+
+// Shared memory: K ring, V ring, P parts, then barriers and the TMEM base.
+constexpr int kOffV = kKStages * kKStageBytes;
+constexpr int kOffP = kOffV + kVStages * kPartBytes;
+constexpr int kOffBars = kOffP + 3 * kPPartBytes;
+constexpr int kNumBars = 3 * kKStages + 2 * kVStages + 5;
+constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;  // + slack to align the ring to 1024 B
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+// Instruction descriptors (kind::f16): BF16 A and B, FP32 accumulator, M = 128.
+//   bits 4-5 D format (1 = F32), 7-9 A format (1 = BF16), 10-12 B format,
+//   15 A major (0 = K), 16 B major (1 = MN), 17-22 N >> 3, 24-28 M >> 4.
+constexpr uint32_t make_idesc(int n, bool b_mn_major) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+           ((uint32_t)(kRows >> 4) << 24);
+}
+constexpr uint32_t kIdescS = make_idesc(kTile, false);  // S[128 x 64] = Q[128 x 128] K[64 x 128]^T
+constexpr uint32_t kIdescO = make_idesc(128, true);     // O_tile[128 x 128] = P[128 x 64] V[64 x 128]
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1:
+// start >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride byte
+// offset >> 4 in 32-45.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+struct alignas(64) ChunkArgs {
+    CUtensorMap kmap;   // 4-D (dim, head, row, batch) or (dim, row, head, batch); box 64 dims x 64 rows
+    CUtensorMap vmap;
+    int kv_rows_inner;  // 1: rows are map dimension 1 (head-major), 0: dimension 2
+    const __nv_bfloat16* q;
+    __nv_bfloat16* out;
+    int64_t q_bstride, q_istride, q_hstride;
+    int64_t o_bstride, o_istride, o_hstride;
+    int seq_len;
+    int first_pos;
+    int n_queries;
+    int n_tiles;
+    float qscale;
+    uint32_t* status;
+    const RopeTable* rope;
+};
+
+// ---- PTX wrappers -----------------------------------------------------------
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16, one CTA.
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+#define GQA_R32(r)                                                                                                 \
+    "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),      \
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),      \
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),     \
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+#define GQA_W32(r)                                                                                                 \
+    "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),    \
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),  \
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),  \
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+
+// 32 consecutive columns of this thread's TMEM lane (warp w reads lanes 32(w%4)..).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : GQA_R32(r)
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        GQA_W32(r)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+
+// Three BF16 parts of an FP32 pair (element a in the low half): x = h + m + l
+// with |x - h - m - l| <= 2^-24 |x| (each residual is exact in FP32).
+__device__ __forceinline__ void split3(float a, float b, uint32_t& h, uint32_t& m, uint32_t& l) {
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(hh);
+    const float ra = a - hf.x, rb = b - hf.y;
+    const __nv_bfloat162 mm = __floats2bfloat162_rn(ra, rb);
+    const float2 mf = __bfloat1622float2(mm);
+    h = bf16x2_bits(hh);
+    m = bf16x2_bits(mm);
+    l = bf16x2_bits(__floats2bfloat162_rn(ra - mf.x, rb - mf.y));
+}
+
+// Bounded wait with one outcome for the whole warp, so that the warp-wide
+// tcgen05.ld / tcgen05.st that follow are never reached by part of it.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+__device__ __forceinline__ void report_timeout(const ChunkArgs& a) {
+    if (a.status) atomicOr(a.status, kDevStatusTimeout);
+}
+
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16, one CTA.
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// ---- the kernel -------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_constant__ ChunkArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // 128-byte swizzle atoms
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
+    uint64_t* kfull = bars;                      // K tile landed       (tx count)
+    uint64_t* krot = kfull + kKStages;           // K parts written     (128 rotation threads)
+    uint64_t* kempty = krot + kKStages;          // S MMAs done with K  (commit)
+    uint64_t* vfull = kempty + kKStages;         // V tile landed       (tx count)
+    uint64_t* vempty = vfull + kVStages;         // O_tile MMAs done    (commit)
+    uint64_t* s_full = vempty + kVStages;        // S(j) in TMEM        (commit)
+    uint64_t* s_free = s_full + 1;               // S(j) read           (128 softmax threads)
+    uint64_t* p_full = s_full + 2;               // P(j) in smem, O_tile(j-1) read (128 softmax threads)
+    uint64_t* pv_done = s_full + 3;              // O_tile(j) complete  (commit)
+    uint64_t* q_ready = s_full + 4;              // Q parts in TMEM     (128 softmax threads)
+    uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+    uint8_t* p_parts = smem + kOffP;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int qh = blockIdx.x;     // Q head
+    const int kvh = qh / kGroup;   // its KV head
+    const int b = blockIdx.y;      // sequence
+    const RopeTable* rt = a.rope;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kKStages; ++s) {
+            mbar_init(&kfull[s], 1);
+            mbar_init(&krot[s], kRotThreads);
+            mbar_init(&kempty[s], 1);
+        }
+        for (int s = 0; s < kVStages; ++s) {
+            mbar_init(&vfull[s], 1);
+            mbar_init(&vempty[s], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, kSoftmaxThreads);
+        mbar_init(p_full, kSoftmaxThreads);
+        mbar_init(pv_done, 1);
+        mbar_init(q_ready, kSoftmaxThreads);
+        fence_barrier_init();
+    }
+    if (warp == kProducerWarp) {  // whole warp: TMEM allocation
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr(tmem_base_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if (lane == 0) {
+            prefetch_tensormap(&a.kmap);
+            prefetch_tensormap(&a.vmap);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_base_slot;
+    const int n_tiles = a.n_tiles;
+
+    if (warp < kSoftmaxWarps) {
+        // ======================= softmax: thread r owns query row r =======================
+        const int r = threadIdx.x;                       // TMEM lane r (warp w: lanes 32w..32w+31)
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        const bool row_ok = r < a.n_queries;
+        const int qpos = a.first_pos + r;
+        const int last_key = row_ok ? min(a.seq_len - 1, qpos) : -1;  // keys 0..last_key are visible
+        bool ok = true;
+
+        // Q row rotated at its position, scaled, split into three parts (TMEM A operand:
+        // dims 2c, 2c+1 in column c of each part).
+        {
+            const __nv_bfloat16* qrow = a.q + (int64_t)b * a.q_bstride + (int64_t)r * a.q_istride +
+                                        (int64_t)qh * a.q_hstride;
+            for (int c8 = 0; c8 < 8; ++c8) {  // pairs 8 c8 .. 8 c8 + 7
+                uint4 xr4 = make_uint4(0u, 0u, 0u, 0u), yr4 = xr4;
+                if (row_ok) {
+                    xr4 = *reinterpret_cast<const uint4*>(qrow + 8 * c8);
+                    yr4 = *reinterpret_cast<const uint4*>(qrow + 64 + 8 * c8);
+                }
+                const uint32_t xw[4] = {xr4.x, xr4.y, xr4.z, xr4.w};
+                const uint32_t yw[4] = {yr4.x, yr4.y, yr4.z, yr4.w};
+                uint32_t part[3][8];  // [part][x columns 0-3, y columns 0-3]
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const float2 x = bf16x2_to_float2(xw[w]), y = bf16x2_to_float2(yw[w]);
+                    const float2 f0 = rope_factor(rt->step[8 * c8 + 2 * w], qpos);
+                    const float2 f1 = rope_factor(rt->step[8 * c8 + 2 * w + 1], qpos);
+                    const float x0 = (x.x * f0.x - y.x * f0.y) * a.qscale;
+                    const float y0 = (x.x * f0.y + y.x * f0.x) * a.qscale;
+                    const float x1 = (x.y * f1.x - y.y * f1.y) * a.qscale;
+                    const float y1 = (x.y * f1.y + y.y * f1.x) * a.qscale;
+                    split3(x0, x1, part[0][w], part[1][w], part[2][w]);
+                    split3(y0, y1, part[0][4 + w], part[1][4 + w], part[2][4 + w]);
+                }
+#pragma unroll
+                for (int pi = 0; pi < 3; ++pi) {  // x dims -> columns 4 c8.., y dims -> columns 32 + 4 c8..
+                    const uint32_t col = kColQ + 64 * pi + 4 * c8;
+                    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(lane_base + col),
+                                 "r"(part[pi][0]), "r"(part[pi][1]), "r"(part[pi][2]), "r"(part[pi][3])
+                                 : "memory");
+                    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                     lane_base + col + 32),
+                                 "r"(part[pi][4]), "r"(part[pi][5]), "r"(part[pi][6]), "r"(part[pi][7])
+                                 : "memory");
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(q_ready);
+        }
+
+        // O(t) = sum over keys of tiles <= t of 2^(s - m(t)) v, kept in TMEM at kColO;
+        // O(t) = O(t-1) * alpha(t) + O_tile(t) with alpha(t) = 2^(m(t-1) - m(t)).
+        auto fold = [&](int t, float alpha) {
+#pragma unroll 1
+            for (int q4 = 0; q4 < 4; ++q4) {
+                uint32_t ot[32], o[32];
+                tmem_ld32(lane_base + kColOT + 32 * q4, ot);
+                if (t > 0) tmem_ld32(lane_base + kColO + 32 * q4, o);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 32; ++c)
+                    o[c] = __float_as_uint(t > 0 ? fmaf(__uint_as_float(o[c]), alpha, __uint_as_float(ot[c]))
+                                                 : __uint_as_float(ot[c]));
+                tmem_st32(lane_base + kColO + 32 * q4, o);
+            }
+        };
+
+        float m_run = -INFINITY;  // running max of the row (log2 units)
+        float l = 0.f;            // running sum of 2^(s - m_run)
+        float alpha_prev = 1.f;   // alpha of the tile whose O_tile is folded next
+        for (int j = 0; j < n_tiles && ok; ++j) {
+            if (!warp_wait(s_full, j & 1)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int k0 = j * kTile;
+            float s[kTile];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+                uint32_t sv[32];
+                tmem_ld32(lane_base + kColS + 32 * h2, sv);
+                tmem_wait_ld();
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const int col = 32 * h2 + c;
+                    s[col] = k0 + col <= last_key ? __uint_as_float(sv[c]) : -INFINITY;
+                    mx = fmaxf(mx, s[col]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(s_free);
+
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);  // 0 for the first visible key
+            m_run = m_new;
+            l *= alpha;
+            if (j > 0) {
+                // O_tile(j-1) is complete and the P buffer is free once O_tile(j-1) is done.
+                if (!warp_wait(pv_done, (j - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                fold(j - 1, alpha_prev);
+            }
+            // P(j) = 2^(s - m_run), split into three parts: row r of each 128-byte-swizzled part.
+            float psum = 0.f;
+#pragma unroll
+            for (int c8 = 0; c8 < kTile / 8; ++c8) {  // keys 8 c8 .. 8 c8 + 7: one 16-byte chunk per part
+                uint32_t ph[4], pm[4], pl[4];
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const int col = 8 * c8 + 2 * w;
+                    const float p0 = s[col] == -INFINITY ? 0.f : exp2f(s[col] - m_run);
+                    const float p1 = s[col + 1] == -INFINITY ? 0.f : exp2f(s[col + 1] - m_run);
+                    psum += p0 + p1;
+                    split3(p0, p1, ph[w], pm[w], pl[w]);
+                }
+                const int off = r * 128 + ((c8 ^ (r & 7)) << 4);
+                *reinterpret_cast<uint4*>(p_parts + off) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+                *reinterpret_cast<uint4*>(p_parts + kPPartBytes + off) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
+                *reinterpret_cast<uint4*>(p_parts + 2 * kPPartBytes + off) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+            }
+            l += psum;
+            alpha_prev = alpha;
+            fence_proxy_async_smem();  // the tensor core reads P through the async proxy
+            tc_fence_before();         // ... after this thread's tcgen05.ld of O_tile(j-1)
+            mbar_arrive(p_full);
+        }
+        if (ok && warp_wait(pv_done, (n_tiles - 1) & 1)) {
+            tc_fence_after();
+            // O = O(n-2) * alpha + O_tile(n-1), then O / l rounded to BF16.
+            __nv_bfloat16* orow =
+                a.out + (int64_t)b * a.o_bstride + (int64_t)r * a.o_istride + (int64_t)qh * a.o_hstride;
+#pragma unroll 1
+            for (int q4 = 0; q4 < 4; ++q4) {
+                uint32_t ot[32], o[32];
+                tmem_ld32(lane_base + kColOT + 32 * q4, ot);
+                if (n_tiles > 1) tmem_ld32(lane_base + kColO + 32 * q4, o);
+                tmem_wait_ld();
+                if (row_ok) {
+#pragma unroll
+                    for (int c = 0; c < 32; c += 8) {
+                        float v8[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const float acc = n_tiles > 1 ? fmaf(__uint_as_float(o[c + e]), alpha_prev,
+                                                                 __uint_as_float(ot[c + e]))
+                                                          : __uint_as_float(ot[c + e]);
+                            v8[e] = acc / l;
+                        }
+                        uint4 w;
+                        w.x = bf16x2_bits(__floats2bfloat162_rn(v8[0], v8[1]));
+                        w.y = bf16x2_bits(__floats2bfloat162_rn(v8[2], v8[3]));
+                        w.z = bf16x2_bits(__floats2bfloat162_rn(v8[4], v8[5]));
+                        w.w = bf16x2_bits(__floats2bfloat162_rn(v8[6], v8[7]));
+                        *reinterpret_cast<uint4*>(orow + 32 * q4 + c) = w;
+                    }
+                }
+            }
+        } else {
+            ok = false;
+        }
+        if (!ok) report_timeout(a);
+    } else if (warp < kSoftmaxWarps + kRotWarps) {
+        // ======================= K rotation + split =======================
+        // Thread t: pairs 8c .. 8c+7 (16-byte chunk c of both 64-dim blocks), keys kq + 16u.
+        const int t = threadIdx.x - kSoftmaxThreads;
+        const int c = t & 7;
+        const int kq = t >> 3;
+        float2 step16[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) step16[i] = rope_factor(rt->step[8 * c + i], 16);
+        bool ok = true;
+        for (int j = 0; j < n_tiles; ++j) {
+            const int st = j % kKStages;
+            if (!mbar_wait(&kfull[st], (j / kKStages) & 1)) {
+                ok = false;
+                break;
+            }
+            uint8_t* kh = smem + st * kKStageBytes;
+            uint8_t* km = kh + kPartBytes;
+            uint8_t* kl = km + kPartBytes;
+            float2 f[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = rope_factor(rt->step[8 * c + i], (int64_t)j * kTile + kq);
+#pragma unroll 1
+            for (int u = 0; u < 4; ++u) {
+                const int k = kq + 16 * u;
+                const int off = k * 128 + ((c ^ (k & 7)) << 4);  // 128-byte swizzle: chunk c of row k
+                const uint4 xv = *reinterpret_cast<const uint4*>(kh + off);
+                const uint4 yv = *reinterpret_cast<const uint4*>(kh + kBlockBytes + off);
+                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+                const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
+                uint32_t xh[4], xm[4], xl[4], yh[4], ym[4], yl[4];
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const float2 x = bf16x2_to_float2(xw[w]), y = bf16x2_to_float2(yw[w]);
+                    const float2 f0 = f[2 * w], f1 = f[2 * w + 1];
+                    split3(x.x * f0.x - y.x * f0.y, x.y * f1.x - y.y * f1.y, xh[w], xm[w], xl[w]);
+                    split3(x.x * f0.y + y.x * f0.x, x.y * f1.y + y.y * f1.x, yh[w], ym[w], yl[w]);
+                }
+                *reinterpret_cast<uint4*>(kh + off) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
+                *reinterpret_cast<uint4*>(kh + kBlockBytes + off) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
+                *reinterpret_cast<uint4*>(km + off) = make_uint4(xm[0], xm[1], xm[2], xm[3]);
+                *reinterpret_cast<uint4*>(km + kBlockBytes + off) = make_uint4(ym[0], ym[1], ym[2], ym[3]);
+                *reinterpret_cast<uint4*>(kl + off) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+                *reinterpret_cast<uint4*>(kl + kBlockBytes + off) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
+                // Factors 16 keys further on.
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float2 g = f[i], sst = step16[i];
+                    f[i] = make_float2(g.x * sst.x - g.y * sst.y, g.x * sst.y + g.y * sst.x);
+                }
+            }
+            fence_proxy_async_smem();  // the tensor core reads these parts through the async proxy
+            mbar_arrive(&krot[st]);
+        }
+        if (!ok) report_timeout(a);
+    } else if (warp == kProducerWarp) {
+        // ======================= TMA producer =======================
+        if (lane == 0) {
+            bool ok = true;
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                const int row = j * kTile;
+                const int c1 = a.kv_rows_inner ? row : kvh;
+                const int c2 = a.kv_rows_inner ? kvh : row;
+                const int ks = j % kKStages;
+                if (j >= kKStages && !mbar_wait(&kempty[ks], ((j / kKStages) - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* kh = smem + ks * kKStageBytes;
+                mbar_arrive_expect_tx(&kfull[ks], kPartBytes);
+                tma_load_4d(kh, &a.kmap, 0, c1, c2, b, &kfull[ks]);
+                tma_load_4d(kh + kBlockBytes, &a.kmap, 64, c1, c2, b, &kfull[ks]);
+                const int vs = j % kVStages;
+                if (j >= kVStages && !mbar_wait(&vempty[vs], ((j / kVStages) - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* vb = smem + kOffV + vs * kPartBytes;
+                mbar_arrive_expect_tx(&vfull[vs], kPartBytes);
+                tma_load_4d(vb, &a.vmap, 0, c1, c2, b, &vfull[vs]);
+                tma_load_4d(vb + kBlockBytes, &a.vmap, 64, c1, c2, b, &vfull[vs]);
+            }
+            if (!ok) report_timeout(a);
+        }
+    } else if (warp == kMmaWarp) {
+        // ======================= MMA issuer =======================
+        if (lane == 0) {
+            bool ok = mbar_wait(q_ready, 0);
+            tc_fence_after();
+            const uint32_t t_s = tmem + kColS, t_ot = tmem + kColOT, t_q = tmem + kColQ;
+            // S(j): products smallest first, (Q part, K part) = (l,h) (m,m) (h,l) (m,h) (h,m) (h,h),
+            // coded as Q part 2,1,0,1,0,0 and K part 0,1,2,0,1,0; 16 dims per MMA.
+            auto issue_s = [&](int j) {
+                uint8_t* kbase = smem + (j % kKStages) * kKStageBytes;
+#pragma unroll
+                for (int pr = 0; pr < 6; ++pr) {
+                    const int qp = (0x001012 >> (4 * pr)) & 0xF;
+                    const int kp = (0x010210 >> (4 * pr)) & 0xF;
+                    const uint32_t kpart = smem_addr(kbase + kp * kPartBytes);
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {  // dims 16kk..: block kk / 4, 32 bytes per step in the row
+                        const uint64_t bd = smem_desc_sw128(kpart + (kk >> 2) * kBlockBytes + (kk & 3) * 32, 16, 1024);
+                        mma_ts(t_s, t_q + 64 * qp + 8 * kk, bd, kIdescS, (pr | kk) != 0);
+                    }
+                }
+                tc_commit(s_full);
+                tc_commit(&kempty[j % kKStages]);
+            };
+            if (ok && n_tiles > 0) {
+                if (mbar_wait(&krot[0], 0)) {
+                    tc_fence_after();
+                    issue_s(0);
+                } else {
+                    ok = false;
+                }
+            }
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                if (j + 1 < n_tiles) {
+                    if (!mbar_wait(&krot[(j + 1) % kKStages], ((j + 1) / kKStages) & 1) || !mbar_wait(s_free, j & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_s(j + 1);
+                }
+                const int vs = j % kVStages;
+                if (!mbar_wait(p_full, j & 1) || !mbar_wait(&vfull[vs], (j / kVStages) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // O_tile(j) = sum over P parts (smallest first) of P_i V: 16 keys per MMA.
+                const uint32_t vaddr = smem_addr(smem + kOffV + vs * kPartBytes);
+#pragma unroll
+                for (int pi = 2; pi >= 0; --pi) {
+                    const uint32_t paddr = smem_addr(p_parts + pi * kPPartBytes);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t ad = smem_desc_sw128(paddr + kk * 32, 16, 1024);
+                        const uint64_t bd = smem_desc_sw128(vaddr + kk * 2048, kBlockBytes, 1024);
+                        mma_ss(t_ot, ad, bd, kIdescO, (pi != 2 || kk != 0) ? 1u : 0u);
+                    }
+                }
+                tc_commit(pv_done);
+                tc_commit(&vempty[vs]);
+            }
+            if (!ok) report_timeout(a);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kProducerWarp) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+}  // namespace
+
+size_t chunked_smem_bytes() { return kSmemBytes; }
+int chunked_max_queries() { return kRows; }
+int chunked_tile_keys() { return kTile; }
+
+cudaError_t chunked_prepare() {
+    return cudaFuncSetAttribute(chunked_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+}
+
+cudaError_t launch_chunked(const ChunkLaunch& l, cudaStream_t stream) {
+    ChunkArgs a;
+    memset(&a, 0, sizeof(a));
+    a.kmap = l.kmap;
+    a.vmap = l.vmap;
+    a.kv_rows_inner = l.kv_rows_inner;
+    a.q = static_cast<const __nv_bfloat16*>(l.q);
+    a.out = static_cast<__nv_bfloat16*>(l.out);
+    a.q_bstride = l.q_bstride;
+    a.q_istride = l.q_istride;
+    a.q_hstride = l.q_hstride;
+    a.o_bstride = l.o_bstride;
+    a.o_istride = l.o_istride;
+    a.o_hstride = l.o_hstride;
+    a.seq_len = l.seq_len;
+    a.first_pos = l.first_pos;
+    a.n_queries = l.n_queries;
+    const int n_keys = l.first_pos + l.n_queries < l.seq_len ? l.first_pos + l.n_queries : l.seq_len;
+    a.n_tiles = (n_keys + kTile - 1) / kTile;
+    a.qscale = l.qscale;
+    a.status = l.status;
+    a.rope = l.rope;
+    chunked_kernel<<<dim3(kNumQHeads, l.batch), kThreads, kSmemBytes, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace gqa

@@ -1,6 +1,7 @@
 // gqa_internal.h -- host-side launch entry points of the kernels (library-internal).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -34,5 +35,25 @@ cudaError_t launch_combine(const float* parts, int n_parts, int64_t part_stride,
                            void* out, int64_t o_bstride, int64_t o_hstride, cudaStream_t stream);
 cudaError_t launch_rope_rows(const void* x, const int32_t* pos, float* out, int rows, const uint64_t* step,
                              cudaStream_t stream);
+
+// Chunked multi-query decode (tensor cores): up to 128 consecutive query
+// positions per sequence, one CTA per (sequence, Q head).
+struct ChunkLaunch {
+    CUtensorMap kmap, vmap;  // 4-D K/V maps, 128-byte swizzle, box 64 dims x 64 rows
+    int kv_rows_inner;
+    const void* q;
+    void* out;
+    int64_t q_bstride, q_istride, q_hstride;
+    int64_t o_bstride, o_istride, o_hstride;
+    int batch, seq_len, first_pos, n_queries;
+    float qscale;
+    uint32_t* status;
+    const RopeTable* rope;
+};
+size_t chunked_smem_bytes();
+int chunked_max_queries();
+int chunked_tile_keys();
+cudaError_t chunked_prepare();
+cudaError_t launch_chunked(const ChunkLaunch& l, cudaStream_t stream);
 
 }  // namespace gqa

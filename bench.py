@@ -10,6 +10,10 @@ One step = one pass of the hot path over one batch of synthetic input:
   config4:           SEQ_LEN=131072; at N>1 GPUs the sequence is split into
                      contiguous shards, FP32 partials are all-gathered over NCCL and
                      merged by the LSE combine kernel (strong scaling).
+  config5:           chunked multi-query decode on the tensor cores: batch 16,
+                     SEQ_LEN=8192, queries 8064..8191 per sequence (causal); the 16
+                     sequences are split across ranks (strong scaling).  Its roofline
+                     line is tensor-bound (algorithmic FLOPs / measured BF16 peak).
 Configs 1-3 shard by sequence: every rank decodes its own sequences, no
 collective (weak scaling).
 
@@ -47,6 +51,15 @@ HEAD_BYTES = 32 * 128 * 2
 def kv_bytes(n_keys: int) -> int:
     """Algorithmic bytes of one sequence's decode: K+V rows of the visible keys, Q and out."""
     return 2 * n_keys * 8 * 128 * 2 + 2 * HEAD_BYTES
+
+
+def peak_bf16():
+    """Dense BF16 tensor peak: the measured burst figure (a kernel timed alone)."""
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(path.read_text())["bf16_tflops"]), "measured burst"
+    except (OSError, ValueError, KeyError):
+        return 1590.0, "fallback"
 
 
 def peak_hbm():
@@ -113,6 +126,8 @@ class Workload:
     name = ""
     scaling = "weak"
     launches_per_step = 1
+    bound = "hbm"
+    flops_per_step = 0
 
     def launch(self, i: int):
         raise NotImplementedError
@@ -334,6 +349,70 @@ class LongContext(Workload):
         return None
 
 
+class ChunkedDecode(Workload):
+    """batch 16, SEQ_LEN=8192, 128 query positions 8064..8191 per
+    sequence, on the tensor cores.  Ranks split the batch (strong scaling)."""
+
+    def __init__(self, device, rank, world, batch=16, seq_len=8192, n_queries=128, seed=20260805):
+        import torch
+        import attention_accelerator_b200 as gqa
+        if batch % world:
+            raise SystemExit(f"config5: batch {batch} does not split over {world} ranks")
+        self.gqa, self.torch = gqa, torch
+        self.S, self.n = seq_len, n_queries
+        self.first = seq_len - n_queries
+        self.local = batch // world
+        self.batch = batch
+        self.name = f"config5_chunked_b{batch}_s{seq_len}"
+        self.scaling = "strong"
+        self.bound = "tensor"
+        vis = sum(t + 1 for t in range(self.first, self.first + n_queries))  # visible keys summed over queries
+        self.bytes_per_step = batch * (2 * seq_len * 8 * 128 * 2 + 2 * n_queries * HEAD_BYTES)
+        self.flops_per_step = batch * 4 * 32 * 128 * vis
+        self.qheads_per_step = batch * n_queries * 32
+        per_set = self.local * 2 * seq_len * 8 * 128 * 2
+        self.nsets = max(2, math.ceil(2 * L2_BYTES / per_set))
+        g = torch.Generator(device=device).manual_seed(seed + 7919 * rank)
+        self.q = [torch.randn((self.local, n_queries, 32, 128), generator=g, device=device).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.k = [torch.randn((self.local, seq_len, 8, 128), generator=g, device=device).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.v = [torch.randn((self.local, seq_len, 8, 128), generator=g, device=device).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.out = torch.empty((self.local, n_queries, 32, 128), dtype=torch.bfloat16, device=device)
+        self.l2_note = f"{self.nsets} rotating buffer sets of {per_set / 2**20:.0f} MiB per rank"
+
+    @property
+    def sets(self):
+        return self.nsets
+
+    def launch(self, i):
+        j = i % self.nsets
+        self.gqa.decode_chunked(self.q[j], self.k[j], self.v[j], first_position=self.first, seq_len=self.S,
+                                out=self.out)
+
+    def config(self):
+        return {"workload": self.name, "batch": self.batch, "batch_per_gpu": self.local, "seq_len": self.S,
+                "queries": f"{self.first}..{self.first + self.n - 1} per sequence (causal)",
+                "kv_layout": "position_major [B,S,8,128] bf16", "l2": self.l2_note,
+                "precision": "Q, K, P each split into three BF16 parts: 6 Q.K + 3 P.V tensor-core products "
+                             "(FP32-equivalent); executed tensor FLOPs = 4.5 x algorithmic"}
+
+    def e2e_inputs(self):
+        return [x.cpu().pin_memory() for x in (self.q[0], self.k[0], self.v[0])]
+
+    def e2e_step(self, host):
+        dev = self.out.device
+        q, k, v = (x.to(dev, non_blocking=True) for x in host)
+        return self.gqa.decode_chunked(q, k, v, first_position=self.first, seq_len=self.S).cpu()
+
+    def oracle_inputs(self):
+        return None
+
+    def gpu_result_set0(self):
+        return None
+
+
 def make_workload(name, device, rank, world, layout="position_major"):
     if name == "config1":
         return SingleDecode(device, rank, 30, 29, uniform=True, layout=layout)
@@ -343,6 +422,8 @@ def make_workload(name, device, rank, world, layout="position_major"):
         return RaggedBatch(device, rank)
     if name == "config4":
         return LongContext(device, rank, world)
+    if name == "config5":
+        return ChunkedDecode(device, rank, world)
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -411,11 +492,44 @@ def e2e_run(torch, wl, steps, device):
     return dt, h2d, d2h
 
 
+def chunked_cpu_sample(n_keys: int, seed: int = 20260805):
+    """One sequence of the config-5 chunk (128 queries at the last positions of n_keys
+    keys) as BF16 codes for the float64 chunked restatement."""
+    import numpy as np
+    import torch
+    g = torch.Generator().manual_seed(seed)
+
+    def bits(t):
+        return t.to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint16)
+    return (bits(torch.randn(1, 128, 32, 128, generator=g)), bits(torch.randn(1, 8, n_keys, 128, generator=g)),
+            bits(torch.randn(1, 8, n_keys, 128, generator=g)))
+
+
+def chunked_cpu_run(budget_s: float, n_keys: int = 8192):
+    """Time oracle/chunked.py (numpy float64, BLAS threads) on whole config-5 sequences."""
+    from oracle.chunked import chunked_golden_f64
+    q, k, v = chunked_cpu_sample(n_keys)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        chunked_golden_f64(q, k, v, n_keys, n_keys - 128)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= budget_s or reps >= 50:
+            return reps, dt
+
+
 def cpu_baseline(wl, budget_s=10.0):
     """Thread-parallel float64 restatement of the golden on this host (kind "port")."""
     import numpy as np
     from oracle import check_rows
     from oracle.parallel import gqa_golden_parallel
+    if isinstance(wl, ChunkedDecode):
+        reps, dt = chunked_cpu_run(budget_s, wl.S)
+        per_seq = wl.bytes_per_step / wl.batch
+        return {"value": round(per_seq * reps / dt / 1e9, 4), "unit": UNIT, "cores": os.cpu_count() or 1,
+                "kind": "port",
+                "sample": f"{reps} x one config-5 sequence (128 queries, SEQ_LEN={wl.S}) by the numpy float64 "
+                          f"chunked restatement (oracle/chunked.py, BLAS on all cores), {dt:.1f} s"}
     inp = wl.oracle_inputs()
     if inp is None:
         # ragged / sharded workloads: time the restatement on a config-2-sized sample
@@ -460,6 +574,24 @@ def reference_arm(args, rank, world):
     import torch
     from concurrent.futures import ThreadPoolExecutor
     from oracle.parallel import gqa_golden_parallel
+    if args.workload == "config5":
+        n_keys = 8192
+        chunked_cpu_run(0.0, n_keys)  # warm-up of one sequence
+        reps, dt = chunked_cpu_run(150.0 / max(1, args.steps + args.warmup) * args.steps, n_keys)
+        per_seq = 2 * n_keys * 8 * 128 * 2 + 2 * 128 * HEAD_BYTES
+        value = per_seq * reps / dt / 1e9
+        sample = (f"{reps} x one config-5 sequence (128 queries 8064..8191, SEQ_LEN=8192) by the numpy float64 "
+                  f"chunked restatement of gen_gqa_wrapper_vectors.py:121-139 (oracle/chunked.py), {dt:.1f} s")
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": reps,
+            "warmup": 1, "ms_per_step": round(dt / reps * 1e3, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic N(0,1) seeded",
+            "impl": "reference", "config": {"workload": "config5", "seq_len": n_keys, "sample_sequences": reps},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
     cfg = {"config1": (30, 29), "config2": (4096, 4095), "config3": (4352, 4351), "config4": (131072, 131071)}
     s, qpos = cfg[args.workload]
     g = torch.Generator().manual_seed(20260805)
@@ -505,7 +637,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("config1", "config2", "config3", "config4"), default="config2")
+    ap.add_argument("--workload", choices=("config1", "config2", "config3", "config4", "config5"), default="config2")
     ap.add_argument("--layout", choices=("position_major", "head_major"), default="position_major")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
@@ -564,6 +696,20 @@ def main():
     tpath = ROOT / "profiles" / f"traffic_{wl.name}.json"
     if tpath.is_file():
         traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+    if wl.bound == "tensor":
+        tpeak, tkind = peak_bf16()
+        per_gpu_flops = wl.flops_per_step if wl.scaling == "weak" else wl.flops_per_step / world
+        tflops = per_gpu_flops / (ms_step * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "achieved": round(tflops, 2), "peak": tpeak, "peak_kind": tkind,
+                    "unit": "TFLOP/s", "frac": round(tflops / tpeak, 4), "traffic": traffic,
+                    "algorithmic_flops_per_launch": per_gpu_flops,
+                    "executed_tensor_tflops": round(4.5 * tflops, 2),
+                    "executed_frac": round(4.5 * tflops / tpeak, 4),
+                    "hbm_gbs": round(achieved, 2)}
+    else:
+        roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind,
+                    "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                    "algorithmic_bytes_per_launch": per_gpu_bytes}
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -574,9 +720,7 @@ def main():
                                                      if wl.scaling == "weak" else wl.config().get("parallelism"))),
             "pct_of_peak_hbm": round(100 * achieved / peak, 2),
             "query_heads_per_s": round(wl.qheads_per_step * scale / (ms_step * 1e-3), 1),
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "algorithmic_bytes_per_launch": per_gpu_bytes},
+            "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": args.e2e_steps},

@@ -218,6 +218,40 @@ int gqa_combine_partials(const float *partials, int n_parts, int64_t part_stride
                          int64_t out_batch_stride, int64_t out_head_stride, void *stream);
 
 /*
+ * Chunked multi-query decode (tensor cores).  For each of `batch` sequences,
+ * n_queries (1..128) consecutive query positions first_position ..
+ * first_position + n_queries - 1, each answered exactly as a gqa_decode call
+ * with QUERY_POSITION = that position and SEQ_LEN = p->seq_len (the
+ * equivalence "128 sequential single-position calls" of the reference's
+ * chunked configuration, gen_gqa_wrapper_vectors.py:121-139 per query).
+ *
+ *   Q   : q + b*p->q_batch_stride + i*q_query_stride + qh*p->q_head_stride + d
+ *   K/V : k + b*k_batch_stride + pos*p->k_pos_stride + kh*p->k_head_stride + d
+ *   out : out + b*p->out_batch_stride + i*out_query_stride + qh*p->out_head_stride + d
+ *
+ * p is validated as gqa_validate does with QUERY_POSITION = the last query's
+ * position; p->flags must be 0 and p->mask_out NULL.  The workspace needs
+ * GQA_CHUNKED_WORKSPACE_BYTES bytes whose first 256 are zero (the device
+ * status word, read with gqa_read_status).  No reference counterpart beyond the
+ * per-query golden: the RTL decodes one position per START.
+ */
+typedef struct gqa_chunk_params {
+    uint32_t batch;
+    uint32_t n_queries;
+    uint32_t first_position;
+    uint32_t reserved;          /* must be 0 */
+    int64_t  q_query_stride;    /* elements between consecutive queries of a sequence */
+    int64_t  out_query_stride;
+    int64_t  k_batch_stride;    /* elements between sequences in K and in V */
+    int64_t  v_batch_stride;
+} gqa_chunk_params;
+
+#define GQA_CHUNKED_WORKSPACE_BYTES ((size_t)256)
+
+int gqa_decode_chunked(const void *q, const void *k, const void *v, void *out, const gqa_params *p,
+                       const gqa_chunk_params *c, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * RoPE of `rows` 128-element BF16 rows, row r at positions[r], to FP32 rows:
  * the rotation of rope_unit.v / rope_half_split (gen_gqa_wrapper_vectors.py:25-35)
  * with the same device code the decode kernel uses.

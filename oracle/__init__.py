@@ -18,6 +18,7 @@ golden ``.mem`` rows under ``tests/golden/``, produced by
 from .bf16 import (bf16_to_f32, f32_to_bf16, pack_bf16, read_mem, read_mem_array,
                    ulp_distance, unpack_bf16, write_mem)
 from .golden import gqa_golden, gqa_golden_f64, rope_half_split, rope_inv_freq
+from .chunked import chunked_golden, chunked_golden_f64
 from .vectors import ReferenceCase, generate_case
 from .checker import check_rows
 from .rope_rom import rope_phase_rom, rope_sincos_rom
@@ -26,5 +27,5 @@ __all__ = [
     "bf16_to_f32", "f32_to_bf16", "pack_bf16", "unpack_bf16", "read_mem", "read_mem_array",
     "write_mem", "ulp_distance", "gqa_golden", "gqa_golden_f64", "rope_half_split",
     "rope_inv_freq", "ReferenceCase", "generate_case", "check_rows", "rope_phase_rom",
-    "rope_sincos_rom",
+    "rope_sincos_rom", "chunked_golden", "chunked_golden_f64",
 ]

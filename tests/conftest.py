@@ -45,6 +45,26 @@ def torch_to_bits(t) -> np.ndarray:
     return t.detach().contiguous().view(torch.int16).cpu().numpy().astype(np.uint16)
 
 
+def assert_parity(golden, got, tight: int = 2, max_ulp: int = 64):
+    """The reference's rule (<= 64 ULP with the 0x3d exemption,
+    pyfiles/check_gqa_output.py:55-75), then the FP32 bar of this build: <=
+    `tight` ULP wherever the golden is at least 2^-10 of its row's largest
+    magnitude (outputs that nearly cancel carry FP32 rounding of the large
+    terms, a few ULP of a tiny number), and a small mean."""
+    from oracle import check_rows
+    from oracle.bf16 import bf16_to_f32, ulp_distance
+    golden = np.asarray(golden).reshape(-1, 128)
+    got = np.asarray(got).reshape(-1, 128)
+    res = check_rows(golden, got, max_ulp)
+    assert res.passed, res.line()
+    mag = np.abs(bf16_to_f32(golden))
+    big = mag >= np.ldexp(mag.max(axis=-1, keepdims=True), -10)
+    dist = ulp_distance(golden, got)
+    assert int(dist[big].max(initial=0)) <= tight, res.line()
+    assert res.mean_ulp < 0.1, res.line()
+    return res
+
+
 @pytest.fixture(scope="session")
 def cuda_device():
     import torch

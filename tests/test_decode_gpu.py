@@ -13,7 +13,7 @@ import pytest
 import torch
 
 import attention_accelerator_b200 as gqa
-from conftest import GOLDEN, bits_to_torch, case_kwargs, torch_to_bits
+from conftest import GOLDEN, assert_parity, bits_to_torch, case_kwargs, torch_to_bits
 from oracle import check_rows, generate_case, gqa_golden
 from oracle.bf16 import f32_to_bf16, read_mem_array
 from oracle.vectors import rope_kat
@@ -43,22 +43,6 @@ def run_decode(q_bits, k_bits, v_bits, device, *, layout="position_major", **kw)
         k = bits_to_torch(k_bits.transpose(1, 0, 2), device)
         v = bits_to_torch(v_bits.transpose(1, 0, 2), device)
     return torch_to_bits(gqa.decode(q, k, v, layout=layout, **kw))
-
-
-def assert_parity(golden, got, tight=TIGHT_ULP):
-    """The reference's rule (<= 64 ULP with the 0x3d exemption), then our tighter
-    FP32 bar: <= `tight` ULP wherever the golden is at least 2^-10 of its row's
-    largest magnitude (outputs that nearly cancel carry FP32 rounding of the
-    large terms, a few ULP of a tiny number), and a small mean."""
-    from oracle.bf16 import bf16_to_f32, ulp_distance
-    res = check_rows(golden, got, MAX_ULP)
-    assert res.passed, res.line()
-    mag = np.abs(bf16_to_f32(golden))
-    big = mag >= np.ldexp(mag.max(axis=-1, keepdims=True), -10)
-    dist = ulp_distance(golden, got)
-    assert int(dist[big].max(initial=0)) <= tight, res.line()
-    assert res.mean_ulp < 0.1, res.line()
-    return res
 
 
 def _case_names():
