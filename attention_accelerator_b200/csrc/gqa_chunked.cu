@@ -12,32 +12,39 @@
 // Precision.  The reference rule is <= 64 BF16 ULP against a float64 golden
 // with no relative floor: outputs that nearly cancel make it as strict as FP32
 // arithmetic.  One BF16 product per operand pair misses it on ~0.5% of the
-// outputs, so every operand is split into three BF16 parts carrying 24
-// significant bits (x = x_h + x_m + x_l), and the products whose size is at
-// least 2^-24 of the leading one are accumulated in FP32 by the tensor core:
-//   S = sum over (i, j) in {(l,h), (m,m), (h,l), (m,h), (h,m), (h,h)} of Q_i K_j^T
-//   O = sum over i in {l, m, h} of P_i V                    (V is exact in BF16)
-// i.e. nine BF16 MMAs where plain BF16 attention issues two.  The tensor-core
-// accumulator is only trusted over short chains: each 64-key tile's P V goes to
-// a fresh TMEM accumulator (12 MMAs), and the softmax threads fold it into the
-// running output with correctly rounded FP32 FMAs (O = O * 2^(m_old - m_new) +
-// O_tile), which also makes the online-softmax rescale exact and free.
+// outputs, so the rotated Q and K are split into three BF16 parts carrying 24
+// significant bits (x = x_h + x_m + x_l) and the products at least 2^-24 of
+// the leading one are accumulated in FP32 by the tensor core.  The three K
+// parts are stacked as one 192-row B operand, so one k-step of S is three MMAs
+// writing three 48-column blocks of TMEM:
+//   Q_h [K_h; K_m; K_l]  -> [hh | hm | hl]
+//   Q_m [K_h; K_m]       ->      [+mh | +mm]
+//   Q_l K_h              ->             [+lh]
+// and the softmax reads S = (block 2 + block 1) + block 0.  P in [0, 1] is
+// split into three BF16 parts too, and V is exact in BF16.
+// The tensor-core accumulator is only trusted over short chains: each 48-key
+// tile's P V goes to a fresh TMEM accumulator (9 MMAs), and the softmax threads
+// fold it into the running output with correctly rounded FP32 FMAs
+// (O = O * 2^(m_old - m_new) + O_tile), which also makes the online-softmax
+// rescale exact.
 //
 // One CTA per (sequence, Q head): M = 128 query rows (TMEM lanes).
 //   warps 0-3   softmax: thread r owns query row r.  Prologue: Q row r rotated
-//               at its position, scaled by scale*log2(e), split, stored to TMEM
-//               (A operand of S).  Per 64-key tile: S row from TMEM, mask, online
-//               softmax, P split into shared memory (A operand of O_tile), and
-//               the previous tile's O_tile folded into the running O in TMEM.
-//               Epilogue: O / l -> BF16 row.
-//   warps 4-7   K rotation: each 64-key K tile lands (TMA, 128-byte swizzle) in
-//               the part-h buffer; the warps rotate it at the key positions and
-//               write the three parts in place / beside it (B operand of S).
-//   warp 8      TMA producer (2-stage ring of K tiles, 3-stage ring of V tiles)
-//               and TMEM allocator.
-//   warp 9      MMA issuer (one thread): S(j+1) is issued as soon as the
-//               softmax has read S(j), so it overlaps softmax(j); O_tile(j) =
-//               P(j) V(j) follows when P(j) is in shared memory.
+//               at its position, scaled by scale*log2(e), split, stored to
+//               shared memory (A operand of S).  Per 48-key tile: S row from
+//               TMEM, mask, online softmax, P split into TMEM (A operand of
+//               O_tile), and the previous tile's O_tile folded into the running
+//               O in TMEM.  Epilogue: O / l -> BF16 row.
+//   warps 4-7   K rotation: each 48-key K tile lands (TMA, 128-byte swizzle) in
+//               rows 0-47 of its stage; the warps rotate it at the key
+//               positions and write the three parts to rows 0-47 / 48-95 /
+//               96-143 (B operand of S).
+//   warp 8      TMA producer (2-stage rings of K and V tiles), TMEM allocator.
+//   warp 9      MMA issuer (one thread).  tcgen05.mma costs about 65 SM cycles
+//               to issue whatever its size, so every instruction here is as
+//               large as TMEM allows (N = 144/96/48 for S, 128 for O); the
+//               48-key tile is what fits three S blocks, the tile and running
+//               O and three P parts in the 512 TMEM columns.
 #include "gqa_device.cuh"
 #include "gqa_internal.h"
 
@@ -48,14 +55,19 @@ namespace gqa {
 
 namespace {
 
-constexpr int kRows = 128;                       // query rows per CTA
-constexpr int kTile = 64;                        // keys per pipeline tile
-constexpr int kKStages = 2;                      // K ring (three parts per stage)
-constexpr int kVStages = 3;                      // V ring
-constexpr int kBlockBytes = kTile * 128;         // 64 rows x 64 BF16: one 128-byte swizzle span per row
-constexpr int kPartBytes = 2 * kBlockBytes;      // a K part or a V tile: dims 0-63 block, dims 64-127 block
-constexpr int kKStageBytes = 3 * kPartBytes;     // K_h, K_m, K_l
-constexpr int kPPartBytes = kRows * 128;         // one P part: 128 rows x 64 keys BF16
+constexpr int kRows = 128;                      // query rows per CTA
+constexpr int kTile = 48;                       // keys per pipeline tile
+constexpr int kStages = 2;                      // K and V rings
+constexpr int kRowB = 128;                      // one 128-byte swizzle row: 64 BF16
+constexpr int kQBlockBytes = kRows * kRowB;     // 128 query rows x 64 dims
+constexpr int kQPartBytes = 2 * kQBlockBytes;   // dims 0-63 block, dims 64-127 block
+constexpr int kKRows = 3 * kTile;               // K_h, K_m, K_l stacked: 144 rows
+constexpr int kKBlockBytes = kKRows * kRowB;    // 144 rows x 64 dims
+constexpr int kKStageBytes = 2 * kKBlockBytes;  // two dim blocks
+constexpr int kVBlockBytes = kTile * kRowB;     // 48 keys x 64 dims
+static_assert(kTile % 16 == 0 && kKBlockBytes % 1024 == 0 && kVBlockBytes % 1024 == 0,
+              "whole 16-key MMA steps; 128-byte swizzle atoms stay 1024-byte aligned");
+constexpr int kVStageBytes = 2 * kVBlockBytes;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kRotWarps = 4;
 constexpr int kProducerWarp = kSoftmaxWarps + kRotWarps;  // 8
@@ -64,33 +76,36 @@ constexpr int kThreads = (kMmaWarp + 1) * 32;             // 320
 constexpr int kRotThreads = kRotWarps * 32;
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 
-// TMEM columns (32-bit, 128 lanes): running O, the tile accumulator O_tile,
-// the S accumulator, and the Q parts (A operand: 128 dims = 64 columns of BF16
-// pairs each).
+// TMEM columns (32-bit, 128 lanes): the three S blocks, the tile accumulator
+// O_tile, the running O, and the three P parts (A operand: 48 keys = 24 columns
+// of BF16 pairs each); every region starts on a 32-column boundary.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 0;
-constexpr uint32_t kColOT = 128;
-constexpr uint32_t kColS = 256;
-constexpr uint32_t kColQ = 320;
-static_assert(kColQ + 3 * 64 <= kTmemCols, "TMEM budget");
+constexpr uint32_t kColS = 0;             // 3 x 48 columns
+constexpr uint32_t kColOT = 160;
+constexpr uint32_t kColO = kColOT + 128;  // 288
+constexpr uint32_t kColP = kColO + 128;   // 416
+constexpr uint32_t kPStride = 32;         // one P part per 32 columns (24 used)
+static_assert(kColS + 3 * kTile <= kColOT && kColP + 2 * kPStride + kTile / 2 <= kTmemCols, "TMEM budget");
 
-// Shared memory: K ring, V ring, P parts, then barriers and the TMEM base.
-constexpr int kOffV = kKStages * kKStageBytes;
-constexpr int kOffP = kOffV + kVStages * kPartBytes;
-constexpr int kOffBars = kOffP + 3 * kPPartBytes;
-constexpr int kNumBars = 3 * kKStages + 2 * kVStages + 5;
-constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;  // + slack to align the ring to 1024 B
+// Shared memory: Q parts, K ring, V ring, then barriers and the TMEM base.
+constexpr int kOffK = 3 * kQPartBytes;
+constexpr int kOffV = kOffK + kStages * kKStageBytes;
+constexpr int kOffBars = kOffV + kStages * kVStageBytes;
+constexpr int kNumBars = 5 * kStages + 5;
+constexpr int kSmemBytes = kOffBars + kNumBars * 8 + 16 + 1024;  // + slack to align to 1024 B
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 // Instruction descriptors (kind::f16): BF16 A and B, FP32 accumulator, M = 128.
 //   bits 4-5 D format (1 = F32), 7-9 A format (1 = BF16), 10-12 B format,
 //   15 A major (0 = K), 16 B major (1 = MN), 17-22 N >> 3, 24-28 M >> 4.
-constexpr uint32_t make_idesc(int n, bool b_mn_major) {
+__host__ __device__ constexpr uint32_t make_idesc(int n, bool b_mn_major) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
            ((uint32_t)(kRows >> 4) << 24);
 }
-constexpr uint32_t kIdescS = make_idesc(kTile, false);  // S[128 x 64] = Q[128 x 128] K[64 x 128]^T
-constexpr uint32_t kIdescO = make_idesc(128, true);     // O_tile[128 x 128] = P[128 x 64] V[64 x 128]
+constexpr uint32_t kIdescS192 = make_idesc(3 * kTile, false);  // Q_h [K_h; K_m; K_l]^T
+constexpr uint32_t kIdescS128 = make_idesc(2 * kTile, false);  // Q_m [K_h; K_m]^T
+constexpr uint32_t kIdescS64 = make_idesc(kTile, false);       // Q_l K_h^T
+constexpr uint32_t kIdescO = make_idesc(128, true);            // O_tile[128 x 128] (+)= P[128 x 48] V[48 x 128]
 
 // Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), version 1:
 // start >> 4 in bits 0-13, leading byte offset >> 4 in 16-29, stride byte
@@ -174,6 +189,38 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+// 2^x for x <= 0 with one MUFU.EX2 (PTX ex2.approx.ftz: relative error below 2^-22,
+// results below 2^-126 flushed to zero, which only drops weights under 2^-126 of the row max).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -194,6 +241,19 @@ __device__ __forceinline__ void split3(float a, float b, uint32_t& h, uint32_t& 
 
 // Bounded wait with one outcome for the whole warp, so that the warp-wide
 // tcgen05.ld / tcgen05.st that follow are never reached by part of it.
+// Three BF16 parts of an FP32 pair with one conversion: the first two parts
+// truncate (mask the low 16 bits, so each residual is exact in FP32), the last
+// rounds to nearest even: |x - h - m - l| <= 2^-22 |x|.  Fewer F2F conversions
+// than split3 for the per-tile operands (P and K).
+__device__ __forceinline__ void split3_fast(float a, float b, uint32_t& h, uint32_t& m, uint32_t& l) {
+    const uint32_t ha = __float_as_uint(a) & 0xFFFF0000u, hb = __float_as_uint(b) & 0xFFFF0000u;
+    h = __byte_perm(ha, hb, 0x7632);
+    const float ra = a - __uint_as_float(ha), rb = b - __uint_as_float(hb);
+    const uint32_t ma = __float_as_uint(ra) & 0xFFFF0000u, mb = __float_as_uint(rb) & 0xFFFF0000u;
+    m = __byte_perm(ma, mb, 0x7632);
+    l = bf16x2_bits(__floats2bfloat162_rn(ra - __uint_as_float(ma), rb - __uint_as_float(mb)));
+}
+
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait(bar, parity));
 }
@@ -219,18 +279,18 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // 128-byte swizzle atoms
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBars);
-    uint64_t* kfull = bars;                      // K tile landed       (tx count)
-    uint64_t* krot = kfull + kKStages;           // K parts written     (128 rotation threads)
-    uint64_t* kempty = krot + kKStages;          // S MMAs done with K  (commit)
-    uint64_t* vfull = kempty + kKStages;         // V tile landed       (tx count)
-    uint64_t* vempty = vfull + kVStages;         // O_tile MMAs done    (commit)
-    uint64_t* s_full = vempty + kVStages;        // S(j) in TMEM        (commit)
-    uint64_t* s_free = s_full + 1;               // S(j) read           (128 softmax threads)
-    uint64_t* p_full = s_full + 2;               // P(j) in smem, O_tile(j-1) read (128 softmax threads)
-    uint64_t* pv_done = s_full + 3;              // O_tile(j) complete  (commit)
-    uint64_t* q_ready = s_full + 4;              // Q parts in TMEM     (128 softmax threads)
+    uint64_t* kfull = bars;                 // K tile landed         (tx count)
+    uint64_t* krot = kfull + kStages;       // K parts written       (128 rotation threads)
+    uint64_t* kempty = krot + kStages;      // S MMAs done with K    (commit)
+    uint64_t* vfull = kempty + kStages;     // V tile landed         (tx count)
+    uint64_t* vempty = vfull + kStages;     // O_tile MMAs done with V (commit)
+    uint64_t* s_full = vempty + kStages;    // S(j) in TMEM          (commit)
+    uint64_t* s_free = s_full + 1;          // S(j) read             (128 softmax threads)
+    uint64_t* p_full = s_full + 2;          // P(j) in TMEM, O_tile(j-1) read (128 softmax threads)
+    uint64_t* pv_done = s_full + 3;         // O_tile(j) complete    (commit)
+    uint64_t* q_ready = s_full + 4;         // Q parts in smem       (128 softmax threads)
     uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
-    uint8_t* p_parts = smem + kOffP;
+    uint8_t* q_parts = smem;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -240,12 +300,10 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
     const RopeTable* rt = a.rope;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kKStages; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&kfull[s], 1);
             mbar_init(&krot[s], kRotThreads);
             mbar_init(&kempty[s], 1);
-        }
-        for (int s = 0; s < kVStages; ++s) {
             mbar_init(&vfull[s], 1);
             mbar_init(&vempty[s], 1);
         }
@@ -282,12 +340,12 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
         const int last_key = row_ok ? min(a.seq_len - 1, qpos) : -1;  // keys 0..last_key are visible
         bool ok = true;
 
-        // Q row rotated at its position, scaled, split into three parts (TMEM A operand:
-        // dims 2c, 2c+1 in column c of each part).
+        // Q row rotated at its position, scaled, split into three parts: row r of
+        // each part's two 128-byte-swizzled dim blocks (A operand of S).
         {
             const __nv_bfloat16* qrow = a.q + (int64_t)b * a.q_bstride + (int64_t)r * a.q_istride +
                                         (int64_t)qh * a.q_hstride;
-            for (int c8 = 0; c8 < 8; ++c8) {  // pairs 8 c8 .. 8 c8 + 7
+            for (int c8 = 0; c8 < 8; ++c8) {  // pairs 8 c8 .. 8 c8 + 7: chunk c8 of both dim blocks
                 uint4 xr4 = make_uint4(0u, 0u, 0u, 0u), yr4 = xr4;
                 if (row_ok) {
                     xr4 = *reinterpret_cast<const uint4*>(qrow + 8 * c8);
@@ -295,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
                 }
                 const uint32_t xw[4] = {xr4.x, xr4.y, xr4.z, xr4.w};
                 const uint32_t yw[4] = {yr4.x, yr4.y, yr4.z, yr4.w};
-                uint32_t part[3][8];  // [part][x columns 0-3, y columns 0-3]
+                uint32_t xp[3][4], yp[3][4];
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
                     const float2 x = bf16x2_to_float2(xw[w]), y = bf16x2_to_float2(yw[w]);
@@ -305,42 +363,21 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
                     const float y0 = (x.x * f0.y + y.x * f0.x) * a.qscale;
                     const float x1 = (x.y * f1.x - y.y * f1.y) * a.qscale;
                     const float y1 = (x.y * f1.y + y.y * f1.x) * a.qscale;
-                    split3(x0, x1, part[0][w], part[1][w], part[2][w]);
-                    split3(y0, y1, part[0][4 + w], part[1][4 + w], part[2][4 + w]);
+                    split3(x0, x1, xp[0][w], xp[1][w], xp[2][w]);
+                    split3(y0, y1, yp[0][w], yp[1][w], yp[2][w]);
                 }
+                const int off = r * kRowB + ((c8 ^ (r & 7)) << 4);
 #pragma unroll
-                for (int pi = 0; pi < 3; ++pi) {  // x dims -> columns 4 c8.., y dims -> columns 32 + 4 c8..
-                    const uint32_t col = kColQ + 64 * pi + 4 * c8;
-                    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(lane_base + col),
-                                 "r"(part[pi][0]), "r"(part[pi][1]), "r"(part[pi][2]), "r"(part[pi][3])
-                                 : "memory");
-                    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
-                                     lane_base + col + 32),
-                                 "r"(part[pi][4]), "r"(part[pi][5]), "r"(part[pi][6]), "r"(part[pi][7])
-                                 : "memory");
+                for (int pi = 0; pi < 3; ++pi) {
+                    uint8_t* part = q_parts + pi * kQPartBytes;
+                    *reinterpret_cast<uint4*>(part + off) = make_uint4(xp[pi][0], xp[pi][1], xp[pi][2], xp[pi][3]);
+                    *reinterpret_cast<uint4*>(part + kQBlockBytes + off) =
+                        make_uint4(yp[pi][0], yp[pi][1], yp[pi][2], yp[pi][3]);
                 }
             }
-            tmem_wait_st();
-            tc_fence_before();
+            fence_proxy_async_smem();  // the tensor core reads Q through the async proxy
             mbar_arrive(q_ready);
         }
-
-        // O(t) = sum over keys of tiles <= t of 2^(s - m(t)) v, kept in TMEM at kColO;
-        // O(t) = O(t-1) * alpha(t) + O_tile(t) with alpha(t) = 2^(m(t-1) - m(t)).
-        auto fold = [&](int t, float alpha) {
-#pragma unroll 1
-            for (int q4 = 0; q4 < 4; ++q4) {
-                uint32_t ot[32], o[32];
-                tmem_ld32(lane_base + kColOT + 32 * q4, ot);
-                if (t > 0) tmem_ld32(lane_base + kColO + 32 * q4, o);
-                tmem_wait_ld();
-#pragma unroll
-                for (int c = 0; c < 32; ++c)
-                    o[c] = __float_as_uint(t > 0 ? fmaf(__uint_as_float(o[c]), alpha, __uint_as_float(ot[c]))
-                                                 : __uint_as_float(ot[c]));
-                tmem_st32(lane_base + kColO + 32 * q4, o);
-            }
-        };
 
         float m_run = -INFINITY;  // running max of the row (log2 units)
         float l = 0.f;            // running sum of 2^(s - m_run)
@@ -352,58 +389,96 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
             }
             tc_fence_after();
             const int k0 = j * kTile;
+            // S = (block 2 + block 1) + block 0, in two load batches (one wait each).
             float s[kTile];
             float mx = -INFINITY;
+            {
+                uint32_t b2[kTile], b1[kTile];
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-                uint32_t sv[32];
-                tmem_ld32(lane_base + kColS + 32 * h2, sv);
+                for (int c16 = 0; c16 < kTile / 16; ++c16) {
+                    tmem_ld16(lane_base + kColS + 2 * kTile + 16 * c16, *reinterpret_cast<uint32_t(*)[16]>(&b2[16 * c16]));
+                    tmem_ld16(lane_base + kColS + kTile + 16 * c16, *reinterpret_cast<uint32_t(*)[16]>(&b1[16 * c16]));
+                }
                 tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const int col = 32 * h2 + c;
-                    s[col] = k0 + col <= last_key ? __uint_as_float(sv[c]) : -INFINITY;
-                    mx = fmaxf(mx, s[col]);
+                for (int col = 0; col < kTile; ++col) s[col] = __uint_as_float(b2[col]) + __uint_as_float(b1[col]);
+            }
+            {
+                uint32_t b0[kTile];
+#pragma unroll
+                for (int c16 = 0; c16 < kTile / 16; ++c16)
+                    tmem_ld16(lane_base + kColS + 16 * c16, *reinterpret_cast<uint32_t(*)[16]>(&b0[16 * c16]));
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(s_free);
+                if (k0 + kTile - 1 <= last_key) {  // every key of the tile is visible to this row
+#pragma unroll
+                    for (int col = 0; col < kTile; ++col) {
+                        s[col] += __uint_as_float(b0[col]);
+                        mx = fmaxf(mx, s[col]);
+                    }
+                } else {
+#pragma unroll
+                    for (int col = 0; col < kTile; ++col) {
+                        const float v = s[col] + __uint_as_float(b0[col]);
+                        s[col] = k0 + col <= last_key ? v : -INFINITY;
+                        mx = fmaxf(mx, s[col]);
+                    }
                 }
             }
-            tc_fence_before();
-            mbar_arrive(s_free);
 
             const float m_new = fmaxf(m_run, mx);
             const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);  // 0 for the first visible key
             m_run = m_new;
             l *= alpha;
+            // P(j) = 2^(s - m_run) split into three parts, in registers while O_tile(j-1) may still
+            // be in flight (keys 2c, 2c+1 in column c of each part: the A operand of O_tile).
+            float psum0 = 0.f, psum1 = 0.f;
+            uint32_t pp[3][kTile / 2];
+#pragma unroll
+            for (int c = 0; c < kTile; c += 2) {
+                // ex2(-inf) = 0 for masked keys; rows without any visible key (past
+                // n_queries) produce values that are never written out.
+                const float p0 = fast_exp2(s[c] - m_run);
+                const float p1 = fast_exp2(s[c + 1] - m_run);
+                psum0 += p0;
+                psum1 += p1;
+                split3_fast(p0, p1, pp[0][c >> 1], pp[1][c >> 1], pp[2][c >> 1]);
+            }
+            const float psum = psum0 + psum1;
             if (j > 0) {
-                // O_tile(j-1) is complete and the P buffer is free once O_tile(j-1) is done.
+                // O_tile(j-1) is complete and the P columns are free once O_tile(j-1) is done.
                 if (!warp_wait(pv_done, (j - 1) & 1)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                fold(j - 1, alpha_prev);
             }
-            // P(j) = 2^(s - m_run), split into three parts: row r of each 128-byte-swizzled part.
-            float psum = 0.f;
 #pragma unroll
-            for (int c8 = 0; c8 < kTile / 8; ++c8) {  // keys 8 c8 .. 8 c8 + 7: one 16-byte chunk per part
-                uint32_t ph[4], pm[4], pl[4];
+            for (int pi = 0; pi < 3; ++pi) {
+                tmem_st16(lane_base + kColP + kPStride * pi, *reinterpret_cast<const uint32_t(*)[16]>(&pp[pi][0]));
+                tmem_st8(lane_base + kColP + kPStride * pi + 16, *reinterpret_cast<const uint32_t(*)[8]>(&pp[pi][16]));
+            }
+            if (j > 0) {
+                // The fold of O_tile(j-1) into the running O, in 32-column chunks:
+                //   O(t) = O(t-1) * alpha(t) + O_tile(t),  alpha(t) = 2^(m(t-1) - m(t)).
+#pragma unroll 1
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    uint32_t ot[32], o[32];
+                    tmem_ld32(lane_base + kColOT + 32 * q4, ot);
+                    if (j > 1) tmem_ld32(lane_base + kColO + 32 * q4, o);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    const int col = 8 * c8 + 2 * w;
-                    const float p0 = s[col] == -INFINITY ? 0.f : exp2f(s[col] - m_run);
-                    const float p1 = s[col + 1] == -INFINITY ? 0.f : exp2f(s[col + 1] - m_run);
-                    psum += p0 + p1;
-                    split3(p0, p1, ph[w], pm[w], pl[w]);
+                    for (int c = 0; c < 32; ++c)
+                        o[c] = __float_as_uint(j > 1 ? fmaf(__uint_as_float(o[c]), alpha_prev, __uint_as_float(ot[c]))
+                                                     : __uint_as_float(ot[c]));
+                    tmem_st32(lane_base + kColO + 32 * q4, o);
                 }
-                const int off = r * 128 + ((c8 ^ (r & 7)) << 4);
-                *reinterpret_cast<uint4*>(p_parts + off) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-                *reinterpret_cast<uint4*>(p_parts + kPPartBytes + off) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
-                *reinterpret_cast<uint4*>(p_parts + 2 * kPPartBytes + off) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
             }
             l += psum;
             alpha_prev = alpha;
-            fence_proxy_async_smem();  // the tensor core reads P through the async proxy
-            tc_fence_before();         // ... after this thread's tcgen05.ld of O_tile(j-1)
+            tmem_wait_st();
+            tc_fence_before();  // P stores and the tcgen05.ld of O_tile(j-1) precede the arrival
             mbar_arrive(p_full);
         }
         if (ok && warp_wait(pv_done, (n_tiles - 1) & 1)) {
@@ -443,32 +518,46 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
         if (!ok) report_timeout(a);
     } else if (warp < kSoftmaxWarps + kRotWarps) {
         // ======================= K rotation + split =======================
-        // Thread t: pairs 8c .. 8c+7 (16-byte chunk c of both 64-dim blocks), keys kq + 16u.
+        // Thread t: pairs 8c .. 8c+7 (16-byte chunk c of both dim blocks), keys kq + 16u, u < 3.
         const int t = threadIdx.x - kSoftmaxThreads;
         const int c = t & 7;
         const int kq = t >> 3;
-        float2 step16[8];
+        // Factors of this thread's pairs at its first key of the tile: exact every
+        // kReanchorTiles tiles, otherwise the previous tile's times e^{i theta 48}.
+        constexpr int kReanchorTiles = 2;
+        float2 step16[8], step_tile[8], base[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) step16[i] = rope_factor(rt->step[8 * c + i], 16);
+        for (int i = 0; i < 8; ++i) {
+            step16[i] = rope_factor(rt->step[8 * c + i], 16);
+            step_tile[i] = rope_factor(rt->step[8 * c + i], kTile);
+        }
         bool ok = true;
         for (int j = 0; j < n_tiles; ++j) {
-            const int st = j % kKStages;
-            if (!mbar_wait(&kfull[st], (j / kKStages) & 1)) {
+            const int st = j % kStages;
+            if (!mbar_wait(&kfull[st], (j / kStages) & 1)) {
                 ok = false;
                 break;
             }
-            uint8_t* kh = smem + st * kKStageBytes;
-            uint8_t* km = kh + kPartBytes;
-            uint8_t* kl = km + kPartBytes;
+            uint8_t* kb = smem + kOffK + st * kKStageBytes;  // dim block 0; block 1 at + kKBlockBytes
             float2 f[8];
+            if (j % kReanchorTiles == 0) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) f[i] = rope_factor(rt->step[8 * c + i], (int64_t)j * kTile + kq);
+                for (int i = 0; i < 8; ++i) base[i] = rope_factor(rt->step[8 * c + i], (int64_t)j * kTile + kq);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float2 g = base[i], st1 = step_tile[i];
+                    base[i] = make_float2(g.x * st1.x - g.y * st1.y, g.x * st1.y + g.y * st1.x);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = base[i];
 #pragma unroll 1
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < kTile / 16; ++u) {
                 const int k = kq + 16 * u;
-                const int off = k * 128 + ((c ^ (k & 7)) << 4);  // 128-byte swizzle: chunk c of row k
-                const uint4 xv = *reinterpret_cast<const uint4*>(kh + off);
-                const uint4 yv = *reinterpret_cast<const uint4*>(kh + kBlockBytes + off);
+                const int off = k * kRowB + ((c ^ (k & 7)) << 4);  // 128-byte swizzle: chunk c of row k
+                const uint4 xv = *reinterpret_cast<const uint4*>(kb + off);
+                const uint4 yv = *reinterpret_cast<const uint4*>(kb + kKBlockBytes + off);
                 const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
                 const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w};
                 uint32_t xh[4], xm[4], xl[4], yh[4], ym[4], yl[4];
@@ -476,15 +565,19 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
                 for (int w = 0; w < 4; ++w) {
                     const float2 x = bf16x2_to_float2(xw[w]), y = bf16x2_to_float2(yw[w]);
                     const float2 f0 = f[2 * w], f1 = f[2 * w + 1];
-                    split3(x.x * f0.x - y.x * f0.y, x.y * f1.x - y.y * f1.y, xh[w], xm[w], xl[w]);
-                    split3(x.x * f0.y + y.x * f0.x, x.y * f1.y + y.y * f1.x, yh[w], ym[w], yl[w]);
+                    split3_fast(x.x * f0.x - y.x * f0.y, x.y * f1.x - y.y * f1.y, xh[w], xm[w], xl[w]);
+                    split3_fast(x.x * f0.y + y.x * f0.x, x.y * f1.y + y.y * f1.x, yh[w], ym[w], yl[w]);
                 }
-                *reinterpret_cast<uint4*>(kh + off) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
-                *reinterpret_cast<uint4*>(kh + kBlockBytes + off) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
-                *reinterpret_cast<uint4*>(km + off) = make_uint4(xm[0], xm[1], xm[2], xm[3]);
-                *reinterpret_cast<uint4*>(km + kBlockBytes + off) = make_uint4(ym[0], ym[1], ym[2], ym[3]);
-                *reinterpret_cast<uint4*>(kl + off) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
-                *reinterpret_cast<uint4*>(kl + kBlockBytes + off) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
+                // Row k of K_h, row 48 + k of K_m, row 96 + k of K_l (the row swizzle is the same:
+                // 48 and 96 are multiples of 8).
+                constexpr int kPartRows = kTile * kRowB;
+                *reinterpret_cast<uint4*>(kb + off) = make_uint4(xh[0], xh[1], xh[2], xh[3]);
+                *reinterpret_cast<uint4*>(kb + kKBlockBytes + off) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
+                *reinterpret_cast<uint4*>(kb + kPartRows + off) = make_uint4(xm[0], xm[1], xm[2], xm[3]);
+                *reinterpret_cast<uint4*>(kb + kKBlockBytes + kPartRows + off) = make_uint4(ym[0], ym[1], ym[2], ym[3]);
+                *reinterpret_cast<uint4*>(kb + 2 * kPartRows + off) = make_uint4(xl[0], xl[1], xl[2], xl[3]);
+                *reinterpret_cast<uint4*>(kb + kKBlockBytes + 2 * kPartRows + off) =
+                    make_uint4(yl[0], yl[1], yl[2], yl[3]);
                 // Factors 16 keys further on.
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -504,24 +597,23 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
                 const int row = j * kTile;
                 const int c1 = a.kv_rows_inner ? row : kvh;
                 const int c2 = a.kv_rows_inner ? kvh : row;
-                const int ks = j % kKStages;
-                if (j >= kKStages && !mbar_wait(&kempty[ks], ((j / kKStages) - 1) & 1)) {
+                const int st = j % kStages;
+                if (j >= kStages && !mbar_wait(&kempty[st], ((j / kStages) - 1) & 1)) {
                     ok = false;
                     break;
                 }
-                uint8_t* kh = smem + ks * kKStageBytes;
-                mbar_arrive_expect_tx(&kfull[ks], kPartBytes);
-                tma_load_4d(kh, &a.kmap, 0, c1, c2, b, &kfull[ks]);
-                tma_load_4d(kh + kBlockBytes, &a.kmap, 64, c1, c2, b, &kfull[ks]);
-                const int vs = j % kVStages;
-                if (j >= kVStages && !mbar_wait(&vempty[vs], ((j / kVStages) - 1) & 1)) {
+                uint8_t* kb = smem + kOffK + st * kKStageBytes;
+                mbar_arrive_expect_tx(&kfull[st], 2 * kVBlockBytes);
+                tma_load_4d(kb, &a.kmap, 0, c1, c2, b, &kfull[st]);                 // rows 0-47, dims 0-63
+                tma_load_4d(kb + kKBlockBytes, &a.kmap, 64, c1, c2, b, &kfull[st]);  // rows 0-47, dims 64-127
+                if (j >= kStages && !mbar_wait(&vempty[st], ((j / kStages) - 1) & 1)) {
                     ok = false;
                     break;
                 }
-                uint8_t* vb = smem + kOffV + vs * kPartBytes;
-                mbar_arrive_expect_tx(&vfull[vs], kPartBytes);
-                tma_load_4d(vb, &a.vmap, 0, c1, c2, b, &vfull[vs]);
-                tma_load_4d(vb + kBlockBytes, &a.vmap, 64, c1, c2, b, &vfull[vs]);
+                uint8_t* vb = smem + kOffV + st * kVStageBytes;
+                mbar_arrive_expect_tx(&vfull[st], kVStageBytes);
+                tma_load_4d(vb, &a.vmap, 0, c1, c2, b, &vfull[st]);
+                tma_load_4d(vb + kVBlockBytes, &a.vmap, 64, c1, c2, b, &vfull[st]);
             }
             if (!ok) report_timeout(a);
         }
@@ -530,24 +622,23 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
         if (lane == 0) {
             bool ok = mbar_wait(q_ready, 0);
             tc_fence_after();
-            const uint32_t t_s = tmem + kColS, t_ot = tmem + kColOT, t_q = tmem + kColQ;
-            // S(j): products smallest first, (Q part, K part) = (l,h) (m,m) (h,l) (m,h) (h,m) (h,h),
-            // coded as Q part 2,1,0,1,0,0 and K part 0,1,2,0,1,0; 16 dims per MMA.
+            const uint32_t t_s = tmem + kColS, t_ot = tmem + kColOT, t_p = tmem + kColP;
+            const uint32_t qh_addr = smem_addr(q_parts);
+            // S(j), 16 dims per k-step kk (dim block kk / 4, 32 bytes per step within the row).
             auto issue_s = [&](int j) {
-                uint8_t* kbase = smem + (j % kKStages) * kKStageBytes;
+                const uint32_t kaddr = smem_addr(smem + kOffK + (j % kStages) * kKStageBytes);
 #pragma unroll
-                for (int pr = 0; pr < 6; ++pr) {
-                    const int qp = (0x001012 >> (4 * pr)) & 0xF;
-                    const int kp = (0x010210 >> (4 * pr)) & 0xF;
-                    const uint32_t kpart = smem_addr(kbase + kp * kPartBytes);
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {  // dims 16kk..: block kk / 4, 32 bytes per step in the row
-                        const uint64_t bd = smem_desc_sw128(kpart + (kk >> 2) * kBlockBytes + (kk & 3) * 32, 16, 1024);
-                        mma_ts(t_s, t_q + 64 * qp + 8 * kk, bd, kIdescS, (pr | kk) != 0);
-                    }
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t koff = (kk >> 2) * kKBlockBytes + (kk & 3) * 32;
+                    const uint32_t qoff = (kk >> 2) * kQBlockBytes + (kk & 3) * 32;
+                    const uint64_t bd = smem_desc_sw128(kaddr + koff, 16, 1024);
+                    mma_ss(t_s, smem_desc_sw128(qh_addr + qoff, 16, 1024), bd, kIdescS192, kk != 0);
+                    mma_ss(t_s + kTile, smem_desc_sw128(qh_addr + kQPartBytes + qoff, 16, 1024), bd, kIdescS128, 1u);
+                    mma_ss(t_s + 2 * kTile, smem_desc_sw128(qh_addr + 2 * kQPartBytes + qoff, 16, 1024), bd,
+                           kIdescS64, 1u);
                 }
                 tc_commit(s_full);
-                tc_commit(&kempty[j % kKStages]);
+                tc_commit(&kempty[j % kStages]);
             };
             if (ok && n_tiles > 0) {
                 if (mbar_wait(&krot[0], 0)) {
@@ -559,33 +650,31 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
             }
             for (int j = 0; j < n_tiles && ok; ++j) {
                 if (j + 1 < n_tiles) {
-                    if (!mbar_wait(&krot[(j + 1) % kKStages], ((j + 1) / kKStages) & 1) || !mbar_wait(s_free, j & 1)) {
+                    if (!mbar_wait(&krot[(j + 1) % kStages], ((j + 1) / kStages) & 1) || !mbar_wait(s_free, j & 1)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     issue_s(j + 1);
                 }
-                const int vs = j % kVStages;
-                if (!mbar_wait(p_full, j & 1) || !mbar_wait(&vfull[vs], (j / kVStages) & 1)) {
+                const int st = j % kStages;
+                if (!mbar_wait(p_full, j & 1) || !mbar_wait(&vfull[st], (j / kStages) & 1)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                // O_tile(j) = sum over P parts (smallest first) of P_i V: 16 keys per MMA.
-                const uint32_t vaddr = smem_addr(smem + kOffV + vs * kPartBytes);
+                // O_tile(j) = P_l V + P_m V + P_h V: 16 keys per MMA (16 rows of 128 bytes).
+                const uint32_t vaddr = smem_addr(smem + kOffV + st * kVStageBytes);
 #pragma unroll
                 for (int pi = 2; pi >= 0; --pi) {
-                    const uint32_t paddr = smem_addr(p_parts + pi * kPPartBytes);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t ad = smem_desc_sw128(paddr + kk * 32, 16, 1024);
-                        const uint64_t bd = smem_desc_sw128(vaddr + kk * 2048, kBlockBytes, 1024);
-                        mma_ss(t_ot, ad, bd, kIdescO, (pi != 2 || kk != 0) ? 1u : 0u);
+                    for (int kk = 0; kk < kTile / 16; ++kk) {
+                        const uint64_t bd = smem_desc_sw128(vaddr + kk * 16 * kRowB, kVBlockBytes, 1024);
+                        mma_ts(t_ot, t_p + kPStride * pi + 8 * kk, bd, kIdescO, (pi != 2 || kk != 0) ? 1u : 0u);
                     }
                 }
                 tc_commit(pv_done);
-                tc_commit(&vempty[vs]);
+                tc_commit(&vempty[st]);
             }
             if (!ok) report_timeout(a);
         }
