@@ -413,7 +413,7 @@ class ChunkedDecode(Workload):
         return None
 
 
-def make_workload(name, device, rank, world, layout="position_major"):
+def make_workload(name, device, rank, world, layout="position_major", chunk_batch=16):
     if name == "config1":
         return SingleDecode(device, rank, 30, 29, uniform=True, layout=layout)
     if name == "config2":
@@ -423,7 +423,7 @@ def make_workload(name, device, rank, world, layout="position_major"):
     if name == "config4":
         return LongContext(device, rank, world)
     if name == "config5":
-        return ChunkedDecode(device, rank, world)
+        return ChunkedDecode(device, rank, world, batch=chunk_batch)
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -642,6 +642,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chunk-batch", type=int, default=16,
+                    help="config5 sequences (16 is the BASELINE config; smaller only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -663,7 +665,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
         build_library()
-    wl = make_workload(args.workload, device, rank, world, args.layout)
+    wl = make_workload(args.workload, device, rank, world, args.layout, args.chunk_batch)
     stream = torch.cuda.Stream(device)
     sampler = ClockSampler(local) if rank == 0 else None
     ms, window = timed_graph_run(torch, wl, args.steps, args.warmup, stream, dist_on)
