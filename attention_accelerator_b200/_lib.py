@@ -71,6 +71,7 @@ class GqaChunkParams(ctypes.Structure):
 
 
 CHUNKED_WORKSPACE_BYTES = 256
+PEER_HANDLE_BYTES = 64
 CHUNKED_MAX_QUERIES = 128
 
 _P = ctypes.c_void_p
@@ -89,6 +90,15 @@ _SIGNATURES = {
                                           _P, ctypes.c_int, _P, ctypes.c_size_t, _P]),
     "gqa_decode_chunked": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), ctypes.POINTER(GqaChunkParams),
                                           _P, ctypes.c_size_t, _P]),
+    "gqa_peer_buffer_bytes": (ctypes.c_size_t, [ctypes.c_int]),
+    "gqa_peer_buffer_create": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "gqa_peer_buffer_open": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "gqa_peer_buffer_close": (ctypes.c_int, [_P]),
+    "gqa_peer_buffer_destroy": (ctypes.c_int, [_P]),
+    "gqa_combine_peers": (ctypes.c_int, [_P, ctypes.c_int64, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
+                                         ctypes.c_int64, ctypes.c_int64, _P, _P]),
+    "gqa_decode_exchange": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), ctypes.POINTER(GqaSeqDesc), _P,
+                                           ctypes.c_int, ctypes.c_int, _P, ctypes.c_size_t, _P]),
     "gqa_combine_partials": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _P,
                                             ctypes.c_int64, ctypes.c_int64, _P]),
     "gqa_rope_rows": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_float, _P]),

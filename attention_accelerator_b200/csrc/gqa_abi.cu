@@ -212,7 +212,7 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // <= 16 splits merged inside one cluster per KV head when the device holds all
 // 8 such clusters at once and that costs fewer tiles per CTA than the one-wave
 // plan with its last-split merge.
-Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = false) {
+Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = false, bool clusters_ok = true) {
     const int slots = sms / gqa::kNumKVHeads > 0 ? sms / gqa::kNumKVHeads : 1;
     int64_t total = 0, longest = 0;
     for (int b = 0; b < batch; ++b) {
@@ -264,7 +264,7 @@ Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = f
             const int c = round8(std::max<int64_t>(kMinChunk, (longest + n - 1) / n));
             const int ns = (int)splits_for(c);
             const double cost = tiles(c) + kClusterMergeTiles;
-            if (ns >= 2 && cost < best && cluster_capacity(ns) >= gqa::kNumKVHeads) {
+            if (clusters_ok && ns >= 2 && cost < best && cluster_capacity(ns) >= gqa::kNumKVHeads) {
                 best = cost;
                 pl.chunk = c;
                 pl.total_splits = ns;
@@ -411,7 +411,9 @@ size_t gqa_workspace_bytes(const gqa_params* p, const gqa_seq_desc* descs, int b
     const gqa::SeqDesc* d = reinterpret_cast<const gqa::SeqDesc*>(descs);
     for (int b = 0; b < batch; ++b)
         if (check_desc(d[b], false) != GQA_OK) return 0;
-    return make_plan(d, batch, sms).ws_bytes;
+    if (batch > 1) return make_plan(d, batch, sms).ws_bytes;
+    // One sequence: enough for gqa_decode_batched and for gqa_decode_exchange (no clusters).
+    return std::max(make_plan(d, 1, sms, true).ws_bytes, make_plan(d, 1, sms, true, false).ws_bytes);
 }
 
 int gqa_decode_plan(const gqa_params* p, const gqa_seq_desc* descs, int batch, int* splits, int* keys_per_split,
@@ -434,7 +436,7 @@ int gqa_decode_plan(const gqa_params* p, const gqa_seq_desc* descs, int batch, i
             st = check_desc(d[b], false);
             if (st != GQA_OK) return st;
         }
-        pl = make_plan(d, batch, sms);
+        pl = make_plan(d, batch, sms, batch == 1);
     }
     *splits = pl.total_splits;
     *keys_per_split = pl.chunk;
@@ -486,15 +488,56 @@ int gqa_decode_batched(const void* q, const void* k, const void* v, void* out, c
     int sms = 0;
     st = current_device(&sms);
     if (st != GQA_OK) return st;
-    const Plan pl = make_plan(d, batch, sms);
+    // One sequence (e.g. this GPU's shard of a long context) takes the single-
+    // sequence plan: splits merged in-kernel, no split-merge launch.
+    const Plan pl = make_plan(d, batch, sms, batch == 1);
     if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
     gqa::DecodeArgs a;
     st = fill_args(a, q, k, v, out, p, workspace, pl, batch);
     if (st != GQA_OK) return st;
-    a.descs = reinterpret_cast<const gqa::SeqDesc*>(dev_descs);
+    a.descs = batch == 1 ? nullptr : reinterpret_cast<const gqa::SeqDesc*>(dev_descs);
     a.single = d[0];
+    if (batch == 1) {
+        a.cluster = pl.cluster;
+        if (pl.cluster == 0 && pl.total_splits > 1 && pl.total_splits <= gqa::decode_last_merge_max_splits())
+            a.ws_arrivals = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + kWsArrivalsOffset);
+    }
     if (gqa::launch_decode(a, pl.total_splits, static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return GQA_ERR_CUDA;
+    return GQA_OK;
+}
+
+int gqa_decode_exchange(const void* q, const void* k, const void* v, void* out, const gqa_params* p,
+                        const gqa_seq_desc* shard, const void* const* peer_buffers, int world, int rank, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    if (!p || !shard || !peer_buffers) return GQA_ERR_NULL_POINTER;
+    if (world < 2 || world > gqa::kMaxPeers || rank < 0 || rank >= world) return GQA_ERR_BATCH;
+    int st = check_geometry(p);
+    if (st != GQA_OK) return st;
+    if (p->flags != 0) return GQA_ERR_BATCH;  // the exchange writes the final BF16 rows
+    st = check_layout(q, k, v, out, p);
+    if (st != GQA_OK) return st;
+    const gqa::SeqDesc d = *reinterpret_cast<const gqa::SeqDesc*>(shard);
+    st = check_desc(d, false);
+    if (st != GQA_OK) return st;
+    int sms = 0;
+    st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    const Plan pl = make_plan(&d, 1, sms, true, false);  // single-sequence plan, no clusters
+    if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
+    gqa::DecodeArgs a;
+    st = fill_args(a, q, k, v, out, p, workspace, pl, 1);
+    if (st != GQA_OK) return st;
+    a.descs = nullptr;
+    a.single = d;
+    if (pl.total_splits > 1) {
+        if (pl.total_splits > gqa::decode_last_merge_max_splits()) return GQA_ERR_KV_RANGE;
+        a.ws_arrivals = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + kWsArrivalsOffset);
+    }
+    a.peer_bases = reinterpret_cast<const uint64_t*>(peer_buffers);
+    a.world = world;
+    a.rank = rank;
+    if (gqa::launch_decode(a, pl.total_splits, static_cast<cudaStream_t>(stream)) != cudaSuccess) return GQA_ERR_CUDA;
     return GQA_OK;
 }
 

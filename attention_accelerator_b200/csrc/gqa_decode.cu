@@ -253,8 +253,106 @@ __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_re
 
 constexpr int kLastMergeScratchFloats = kGroup * kLastMergeMaxSplits + 2 * kGroup;
 
+// Long-context split across GPUs, fused into the decode: the CTA that holds
+// this rank's merged rows of Q heads 4h..4h+3 (acc[128], m, l in shared
+// memory) pushes them into every rank's exchange buffer (push_rows[e & 1][rank],
+// plain stores over NVLink), releases them at system scope with one flag per
+// (source rank, KV head) = e in each destination, then waits (bounded) for the
+// peers' flags of head h in its OWN buffer and merges the rows it received,
+//   M = max m_r, O = sum 2^(m_r - M) acc_r, L = sum 2^(m_r - M) l_r,
+// writing BF16 O / L; the last of the eight heads advances the epoch.  Pushing
+// puts one one-way NVLink transfer on the critical path instead of remote
+// polling and remote reads.  Rows of epoch e are rewritten at e + 2 only: by
+// then every peer has published e + 1, which it does after finishing epoch e.
+__device__ __forceinline__ void exchange_and_finish(const DecodeArgs& a, int h, int tid, const float* rows,
+                                                    int* info, const OutSpec& direct) {
+    uint8_t* mine = reinterpret_cast<uint8_t*>(a.peer_bases[a.rank]);
+    uint32_t* hdr = reinterpret_cast<uint32_t*>(mine);
+    const size_t push = peer_push_offset(1);
+    if (tid == 0) {
+        info[3] = (int)(*reinterpret_cast<volatile uint32_t*>(hdr) + 1u);
+        info[4] = 1;  // cleared by a wait that gives up
+    }
+    named_barrier_sync(1, kConsumerThreads);
+    const uint32_t e = (uint32_t)info[3];
+    // Row (source rank r, Q head 4h + hq) of parity e & 1 in any rank's push area.
+    auto push_row = [&](uint8_t* base, int r) {
+        return reinterpret_cast<float*>(base + push + kPushFlagsBytes) +
+               (((size_t)(e & 1u) * kMaxPeers + r) * kNumQHeads + (size_t)h * kGroup) * kPartialFloats;
+    };
+    for (int p = 0; p < a.world; ++p) {
+        float* dst = push_row(reinterpret_cast<uint8_t*>(a.peer_bases[p]), a.rank);
+        for (int i = tid; i < kGroup * kPartialFloats; i += kConsumerThreads) dst[i] = rows[i];
+    }
+    named_barrier_sync(1, kConsumerThreads);
+    if (tid == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int p = 0; p < a.world; ++p) {
+            uint32_t* flags = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(a.peer_bases[p]) + push);
+            st_release_sys(flags + a.rank * kNumKVHeads + h, e);
+        }
+    }
+    // Thread r waits for source rank r's flag of head h in this rank's own buffer.
+    if (tid < a.world) {
+        const uint32_t* flag = reinterpret_cast<const uint32_t*>(mine + push) + tid * kNumKVHeads + h;
+        int ok = 1;
+        if ((int)(ld_acquire_sys(flag) - e) < 0) {
+            const long long t0 = clock64();
+            while ((int)(ld_acquire_sys(flag) - e) < 0) {
+                if (clock64() - t0 > kWaitTimeoutCycles) {
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        if (!ok) {
+            atomicOr(a.ws_status, kDevStatusTimeout);
+            info[4] = 0;
+        }
+    }
+    named_barrier_sync(1, kConsumerThreads);
+    const bool all_ok = info[4] != 0;
+    if (all_ok) {
+        for (int o = tid; o < kOutputs; o += kConsumerThreads) {
+            const int hq = o >> 7, dim = o & 127;
+            float mr[kMaxPeers], lr[kMaxPeers], ar[kMaxPeers];
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r) {
+                if (r < a.world) {
+                    const volatile float* row = push_row(mine, r) + hq * kPartialFloats;
+                    mr[r] = row[kHeadDim];
+                    lr[r] = row[kHeadDim + 1];
+                    ar[r] = row[dim];
+                }
+            }
+            float M = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r)
+                if (r < a.world) M = fmaxf(M, mr[r]);
+            const float Mu = M == -INFINITY ? 0.f : M;
+            float L = 0.f, O = 0.f;
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r) {
+                if (r < a.world) {
+                    const float f = exp2f(mr[r] - Mu);
+                    L = fmaf(lr[r], f, L);
+                    O = fmaf(ar[r], f, O);
+                }
+            }
+            write_result(direct, 0, h * kGroup + hq, dim, O, M, L);
+        }
+    }
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(hdr + 1, 1u) == (uint32_t)(kNumKVHeads - 1)) {
+            hdr[1] = 0u;
+            *reinterpret_cast<volatile uint32_t*>(hdr) = e;
+        }
+    }
+}
+
 __device__ __forceinline__ void last_split_merge(const DecodeArgs& a, int n, int h, int tid, float* sh, int* flag,
-                                                 const OutSpec& direct) {
+                                                 const OutSpec& direct, float* xrows, int* info) {
     named_barrier_sync(1, kConsumerThreads);  // every partial store of this CTA is issued
     if (tid == 0) {
         fence_acq_rel_gpu();  // ... and ordered before the arrival (cumulative through the barrier)
@@ -309,17 +407,30 @@ __device__ __forceinline__ void last_split_merge(const DecodeArgs& a, int n, int
         for (int j = 0; j < kMergeBatch; ++j) o4[j & 3] = fmaf(v[j], f[j], o4[j & 3]);  // f[j] = 0 past n
         float rest = 0.f;
         for (int s = kMergeBatch; s < n; ++s) rest = fmaf(__ldcg(p + s * sstride), f[s], rest);
-        write_result(direct, 0, h * kGroup + hq, o & 127, ((o4[0] + o4[1]) + (o4[2] + o4[3])) + rest, tot[2 * hq],
-                     tot[2 * hq + 1]);
+        const float O = ((o4[0] + o4[1]) + (o4[2] + o4[3])) + rest;
+        if (a.world > 1) {  // this rank's merged rows go to the cross-GPU exchange
+            xrows[hq * kPartialFloats + (o & 127)] = O;
+            if ((o & 127) == 0) {
+                xrows[hq * kPartialFloats + kHeadDim] = tot[2 * hq];
+                xrows[hq * kPartialFloats + kHeadDim + 1] = tot[2 * hq + 1];
+            }
+        } else {
+            write_result(direct, 0, h * kGroup + hq, o & 127, O, tot[2 * hq], tot[2 * hq + 1]);
+        }
     };
     finish(tid, v0, p0);
     if (has1) finish(o1, v1, p1);
+    if (a.world > 1) {
+        named_barrier_sync(1, kConsumerThreads);
+        exchange_and_finish(a, h, tid, xrows, info, direct);
+    }
 }
 
 // Epilogue shared memory (in the drained ring): warp partials, the split's merged
 // partial, the last-split merge's scratch, the warp factors.
 static_assert((kConsumerWarps * kGroup * kPartialFloats + kGroup * kPartialFloats + kLastMergeScratchFloats +
-               2 * kConsumerWarps * kGroup + kGroup) * 4 <= kOffBars, "epilogue buffers fit the ring");
+               2 * kConsumerWarps * kGroup + kGroup + kGroup * kPartialFloats) * 4 <= kOffBars,
+              "epilogue buffers fit the ring");
 
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -665,6 +776,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     float* wf = lsm + kLastMergeScratchFloats;  // [w][hq]  2^(m_w - M)
     float* wl = wf + kConsumerWarps * kGroup;   // [w][hq]  l_w * 2^(m_w - M)
     float* wm = wl + kConsumerWarps * kGroup;   // [hq]     M
+    float* xrows = wm + kGroup;                 // [hq][132] this rank's rows for the cross-GPU exchange
+    const bool exchange = a.world > 1;
     // Factors once per (warp, head): thread t < 44 owns warp t / 4, head t % 4.
     if (tid < kConsumerWarps * kGroup) {
         const int hq = tid & 3;
@@ -679,7 +792,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
     named_barrier_sync(1, kConsumerThreads);
     // Thread t < 128 merges head t / 32, dims 4 (t % 32) .. +3.
-    float* part = clustered ? cpart : a.ws_partials + ((int64_t)gsplit * kNumKVHeads + h) * kGroup * kPartialFloats;
+    float* part = clustered                     ? cpart
+                  : (exchange && n_split == 1) ? xrows
+                                               : a.ws_partials + ((int64_t)gsplit * kNumKVHeads + h) * kGroup * kPartialFloats;
     if (tid < kOutputs / 4) {
         const int hq = tid >> 5, d0 = (tid & 31) * 4;
         float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -692,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             L += wl[w * kGroup + hq];
         }
         const float M = wm[hq];
-        if (n_split == 1 && !clustered) {
+        if (n_split == 1 && !clustered && !exchange) {
             write_result4(direct, b, h * kGroup + hq, d0, O, M, L);
         } else {
             float* row = part + hq * kPartialFloats;
@@ -705,8 +820,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
     if (clustered) {
         cluster_merge(a.cluster, gsplit, c, lane, cpart, direct, h);
+    } else if (exchange && n_split == 1) {
+        named_barrier_sync(1, kConsumerThreads);
+        exchange_and_finish(a, h, tid, xrows, info, direct);
     } else if (a.ws_arrivals != nullptr && n_split > 1) {
-        last_split_merge(a, n_split, h, tid, lsm, info + 2, direct);
+        last_split_merge(a, n_split, h, tid, lsm, info + 2, direct, xrows, info);
     }
 }
 

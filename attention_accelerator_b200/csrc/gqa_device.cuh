@@ -105,7 +105,39 @@ struct alignas(64) DecodeArgs {
                             // thread-block cluster and merge through distributed shared memory
     uint32_t* ws_arrivals;  // non-null: single sequence, the last split of each KV head to finish merges
                             // (one arrival counter per KV head, zero between calls)
+    const uint64_t* peer_bases;  // world > 1: this GPU decodes a shard of one sequence and exchanges the
+    int world, rank;             // merged rows with the other ranks' exchange buffers (device array)
 };
+
+// Exchange buffer of the long-context split (one per rank, mapped by the others):
+//   [0] u32 epoch, [4] u32 arrivals, [64] u32 flag[batch * 32], then
+//   float rows[2][batch * 32][132] from peer_data_offset(batch), double-buffered by epoch
+//   parity: the pull exchange of gqa_combine_peers (each rank publishes into its own buffer);
+//   then, from peer_push_offset(batch), the push exchange of the fused decode (one sequence):
+//   u32 push_flag[kMaxPeers][8 KV heads] and float push_rows[2][kMaxPeers][32][132], which
+//   the ranks write into each other's buffers.
+constexpr int kPeerFlagsOffset = 64;
+constexpr int kMaxPeers = 8;
+__host__ __device__ inline size_t peer_data_offset(int batch) {
+    const size_t flags_end = kPeerFlagsOffset + (size_t)batch * kNumQHeads * 4;
+    return (flags_end + 255) & ~(size_t)255;
+}
+__host__ __device__ inline size_t peer_push_offset(int batch) {
+    return peer_data_offset(batch) + 2 * (size_t)batch * kNumQHeads * kPartialFloats * sizeof(float);
+}
+constexpr size_t kPushFlagsBytes = 256;  // kMaxPeers x 8 KV heads x u32
+constexpr size_t kPushRowsBytes = 2 * (size_t)kMaxPeers * kNumQHeads * kPartialFloats * sizeof(float);
+static_assert(kMaxPeers * kNumKVHeads * 4 <= (int)kPushFlagsBytes, "push flags fit");
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // ---------------------------------------------------------------------------
 // PTX wrappers

@@ -56,4 +56,10 @@ int chunked_tile_keys();
 cudaError_t chunked_prepare();
 cudaError_t launch_chunked(const ChunkLaunch& l, cudaStream_t stream);
 
+// Long-context exchange of per-GPU partial rows over peer memory + LSE combine.
+size_t peer_buffer_bytes(int batch);
+cudaError_t launch_combine_peers(const float* local, int64_t part_bstride, const uint64_t* peer_bases, int world,
+                                 int rank, int batch, void* out, int64_t o_bstride, int64_t o_hstride,
+                                 uint32_t* status, cudaStream_t stream);
+
 }  // namespace gqa

@@ -126,6 +126,10 @@ class Workload:
     name = ""
     scaling = "weak"
     launches_per_step = 1
+    graph_ok = False  # multi-launch steps under torch.distributed: graphs only without collectives
+
+    def close(self):
+        pass
     bound = "hbm"
     flops_per_step = 0
 
@@ -274,11 +278,12 @@ class RaggedBatch(Workload):
 class LongContext(Workload):
     """SEQ_LEN=131072; contiguous key shards across ranks + NCCL all-gather."""
 
-    def __init__(self, device, rank, world, seq_len=131072, seed=20260805):
+    def __init__(self, device, rank, world, seq_len=131072, seed=20260805, exchange="fused"):
         import torch
         import attention_accelerator_b200 as gqa
         self.gqa, self.torch = gqa, torch
         self.rank, self.world = rank, world
+        self.exchange = exchange
         self.S = seq_len
         self.name = f"config4_decode_s{seq_len}"
         self.scaling = "strong"
@@ -302,9 +307,17 @@ class LongContext(Workload):
             self.plan = gqa.plan_batch([seq_len], pos_begin=[lo], pos_end=[hi], kv_starts=[0], partial=True,
                                        device=device)
             self.part = torch.empty((1, 32, 132), dtype=torch.float32, device=device)
-            self.gathered = torch.empty((world, 1, 32, 132), dtype=torch.float32, device=device)
             self.out = torch.empty((1, 32, 128), dtype=torch.bfloat16, device=device)
             self.launches_per_step = 2
+            if exchange in ("fused", "peer"):
+                from attention_accelerator_b200.distributed import PeerExchange
+                self.peer = PeerExchange(1, device=device)
+                self.graph_ok = True  # no collective library inside the step
+                if exchange == "fused":
+                    self.launches_per_step = 1
+                    self.plan = gqa.plan_batch([seq_len], pos_begin=[lo], pos_end=[hi], kv_starts=[0], device=device)
+            else:
+                self.gathered = torch.empty((world, 1, 32, 132), dtype=torch.float32, device=device)
         self.l2_note = f"{self.nsets} rotating buffer sets of {per_set / 2**20:.0f} MiB per rank"
 
     @property
@@ -318,15 +331,26 @@ class LongContext(Workload):
                             out=self.out)
             return
         import torch.distributed as dist
+        if self.exchange == "fused":
+            self.peer.decode(self.q[j], self.k[j], self.v[j], self.plan, out=self.out)
+            return
         self.gqa.decode_batch(self.q[j], self.k[j], self.v[j], self.plan, out=self.part)
+        if self.exchange == "peer":
+            self.peer.combine(self.part, out=self.out)  # NVLink peer exchange fused with the LSE combine
+            return
         dist.all_gather_into_tensor(self.gathered.view(self.world, -1), self.part.view(-1))
         self.gqa.combine_partials(self.gathered, out=self.out)  # same as distributed.gather_partials + combine
 
     def config(self):
+        xchg = {"fused": "decode kernel publishes each KV head's merged rows to the NVLink peer exchange, waits for "
+                         "the peers' and writes the merged output (gqa_decode_exchange, one launch per step)",
+                "peer": "NVLink peer-memory exchange of 32x132 FP32 partials fused with the LSE combine "
+                        "(gqa_combine_peers)",
+                "nccl": "NCCL all-gather of 32x132 FP32 partials + LSE combine kernel"}[self.exchange]
         return {"workload": self.name, "batch": 1, "seq_len": self.S, "query_position": self.S - 1,
                 "kv_layout": "position_major shard [S/N,8,128] bf16 per GPU",
-                "parallelism": f"sequence split x{self.world}, NCCL all-gather of 32x132 FP32 partials"
-                if self.world > 1 else "single GPU", "l2": self.l2_note}
+                "parallelism": f"sequence split x{self.world}, {xchg}" if self.world > 1 else "single GPU",
+                "l2": self.l2_note}
 
     def e2e_inputs(self):
         return [x.cpu().pin_memory() for x in (self.q[0], self.k[0], self.v[0])]
@@ -336,11 +360,19 @@ class LongContext(Workload):
         q, k, v = (x.to(dev, non_blocking=True) for x in host)
         if self.world == 1:
             out = self.gqa.decode(q[0], k, v, seq_len=self.S, query_position=self.S - 1)
+        elif self.exchange == "fused":
+            out = self.peer.decode(q, k, v, self.plan)
+        elif self.exchange == "peer":
+            out = self.peer.combine(self.gqa.decode_batch(q, k, v, self.plan))
         else:
             from attention_accelerator_b200.distributed import gather_partials
             part = self.gqa.decode_batch(q, k, v, self.plan)
             out = self.gqa.combine_partials(gather_partials(part))
         return out.cpu()
+
+    def close(self):
+        if getattr(self, "peer", None) is not None:
+            self.peer.close()
 
     def oracle_inputs(self):
         return None
@@ -413,7 +445,7 @@ class ChunkedDecode(Workload):
         return None
 
 
-def make_workload(name, device, rank, world, layout="position_major", chunk_batch=16):
+def make_workload(name, device, rank, world, layout="position_major", chunk_batch=16, exchange="fused"):
     if name == "config1":
         return SingleDecode(device, rank, 30, 29, uniform=True, layout=layout)
     if name == "config2":
@@ -421,7 +453,7 @@ def make_workload(name, device, rank, world, layout="position_major", chunk_batc
     if name == "config3":
         return RaggedBatch(device, rank)
     if name == "config4":
-        return LongContext(device, rank, world)
+        return LongContext(device, rank, world, exchange=exchange)
     if name == "config5":
         return ChunkedDecode(device, rank, world, batch=chunk_batch)
     raise SystemExit(f"unknown workload {name}")
@@ -435,7 +467,7 @@ def timed_graph_run(torch, wl, steps, warmup, stream, dist_on):
             wl.launch(i)
     torch.cuda.synchronize()
     graphs = {}
-    use_graphs = not (dist_on and wl.launches_per_step > 1)
+    use_graphs = not (dist_on and wl.launches_per_step > 1) or wl.graph_ok
 
     def graph_of(n):
         if n not in graphs:
@@ -642,6 +674,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=("fused", "peer", "nccl"), default="fused",
+                    help="config4 at N>1: exchange inside the decode kernel (fused), in a separate combine kernel "
+                         "over peer memory (peer), or NCCL all-gather + combine (nccl)")
     ap.add_argument("--chunk-batch", type=int, default=16,
                     help="config5 sequences (16 is the BASELINE config; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -665,7 +700,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
         build_library()
-    wl = make_workload(args.workload, device, rank, world, args.layout, args.chunk_batch)
+    wl = make_workload(args.workload, device, rank, world, args.layout, args.chunk_batch, args.exchange)
     stream = torch.cuda.Stream(device)
     sampler = ClockSampler(local) if rank == 0 else None
     ms, window = timed_graph_run(torch, wl, args.steps, args.warmup, stream, dist_on)
@@ -732,6 +767,7 @@ def main():
         print(json.dumps(line), flush=True)
     if dist_on:
         torch.distributed.barrier()
+        wl.close()
         torch.distributed.destroy_process_group()
 
 

@@ -141,7 +141,8 @@ int gqa_validate(const gqa_params *p);
  * allocated; every call leaves the counters zero again, and gqa_read_status
  * clears the whole header after a timed-out wait.  The rest needs no
  * initialisation (every call writes its split partials before reading them).
- * Calls that share a workspace must be ordered (one stream).
+ * Calls that share a workspace must be ordered (one stream).  With `descs`
+ * and batch 1 the size also covers gqa_decode_exchange of that shard.
  */
 size_t gqa_workspace_bytes(const gqa_params *p, const gqa_seq_desc *descs, int batch);
 
@@ -151,8 +152,8 @@ size_t gqa_workspace_bytes(const gqa_params *p, const gqa_seq_desc *descs, int b
  * number of key splits, the keys per split, and the cluster size (> 0 when a
  * single sequence's splits of each KV head run as one thread-block cluster and
  * merge on chip; 0 when the last split of each KV head to finish merges them
- * (single sequence) or split_merge_kernel does (batched call)).  Returns a
- * status.
+ * (one sequence, also a batched call of one) or split_merge_kernel does
+ * (batched call of several).  Returns a status.
  */
 int gqa_decode_plan(const gqa_params *p, const gqa_seq_desc *descs, int batch, int *splits, int *keys_per_split,
                     int *cluster);
@@ -266,6 +267,47 @@ int gqa_rope_rows(const void *x, const int32_t *positions, float *out, int rows,
  */
 int gqa_rope_phase_rom(uint32_t *phase, int head_dim, double rope_theta);
 int gqa_rope_sincos_rom(uint32_t *sincos, int addr_bits);
+
+/*
+ * Long-context sequence split across the GPUs of one node: exchange of the
+ * per-GPU FP32 partial rows (GQA_FLAG_PARTIAL_OUT) over NVLink peer memory,
+ * fused with the log-sum-exp combine (no collective library).  Each rank
+ * creates one exchange buffer, shares its CUDA IPC handle with the other ranks
+ * (e.g. over torch.distributed), opens theirs, and passes a DEVICE array of all
+ * `world` buffer pointers (its own at index `rank`) to gqa_combine_peers, which
+ * publishes this rank's partials, waits (bounded, ~1 s) for every peer's, and
+ * writes the merged BF16 rows [batch][32][128] on every rank.  Calls must be
+ * made in the same order on all ranks; the exchange epoch lives in the buffer,
+ * so CUDA-graph replays work.  A timed-out wait sets the workspace status word
+ * (gqa_read_status); the exchange must then be re-created.  batch <= 64 (all
+ * CTAs of the exchange resident at once).  No reference counterpart: the
+ * reference has one device.
+ */
+#define GQA_PEER_HANDLE_BYTES 64
+size_t gqa_peer_buffer_bytes(int batch);
+int gqa_peer_buffer_create(size_t bytes, void **buffer, void *ipc_handle);
+int gqa_peer_buffer_open(const void *ipc_handle, void **buffer);
+int gqa_peer_buffer_close(void *buffer);
+int gqa_peer_buffer_destroy(void *buffer);
+int gqa_combine_peers(const float *partials, int64_t partial_batch_stride, const void *const *peer_buffers,
+                      int world, int rank, int batch, void *out, int64_t out_batch_stride,
+                      int64_t out_head_stride, void *workspace, void *stream);
+
+/*
+ * The same exchange fused into the decode kernel: this rank decodes its shard
+ * `shard` (pos_begin/pos_end of one sequence, as for gqa_decode_batched with
+ * batch 1), and the CTA that merges each KV head's splits publishes the head's
+ * rows to the exchange buffer, waits for the peers' rows over NVLink and writes
+ * the final BF16 rows of the whole sequence to `out` [32][128] on every rank —
+ * one launch per step, no combine kernel.  The rows are pushed into every
+ * rank's buffer and each rank waits on flags in its own memory.  2 <= world <= 8.
+ * `workspace`: gqa_workspace_bytes(p, shard, 1) bytes (the 256-byte header zeroed
+ * at allocation).  p->flags must be 0.  The exchange buffers are those of
+ * gqa_peer_buffer_create (batch 1).
+ */
+int gqa_decode_exchange(const void *q, const void *k, const void *v, void *out, const gqa_params *p,
+                        const gqa_seq_desc *shard, const void *const *peer_buffers, int world, int rank,
+                        void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Read (and clear) the device status word a kernel leaves in `workspace`:

@@ -281,8 +281,10 @@ def test_split_plans(cuda_device):
     for s in (4096, 131072):
         p = gqa.decode_plan(s)
         assert p.cluster == 0 and p.splits > 1 and p.splits * p.keys_per_split >= s
-    batch = gqa.decode_plan(plan=gqa.plan_batch([4096], device=cuda_device))
-    assert batch.cluster == 0 and batch.splits > 1
+    one = gqa.decode_plan(plan=gqa.plan_batch([4096], device=cuda_device))
+    assert one == gqa.decode_plan(4096)  # a batch of one takes the single-sequence plan
+    two = gqa.decode_plan(plan=gqa.plan_batch([4096, 4096], device=cuda_device))
+    assert two.cluster == 0 and two.splits > 2
 
 
 # (seq_len, qpos): 100 / 600 / 1000 keys take the cluster merge, the rest the
@@ -291,15 +293,18 @@ def test_split_plans(cuda_device):
                                           (20000, 19999), (33000, 32999)])
 def test_single_sequence_merges_match_split_merge_kernel(seq_len, qpos, cuda_device):
     """The single-sequence merges (cluster or last split) and split_merge_kernel
-    (a batch of one) agree to FP32 rounding, and both meet the oracle."""
+    (the same sequence twice in one batch) agree to FP32 rounding, and both meet
+    the oracle."""
     assert gqa.decode_plan(seq_len, query_position=qpos).splits > 1
     q, k, v = normal_inputs(seq_len, seed=seq_len + qpos)
     clustered = run_decode(q, k, v, cuda_device, seq_len=seq_len, query_position=qpos)
-    plan = gqa.plan_batch([seq_len], query_positions=[qpos], device=cuda_device)
+    plan = gqa.plan_batch([seq_len, seq_len], query_positions=[qpos, qpos], kv_starts=[0, 0], device=cuda_device)
     assert gqa.decode_plan(plan=plan).cluster == 0
-    merged = torch_to_bits(gqa.decode_batch(bits_to_torch(q[None], cuda_device),
-                                            bits_to_torch(k.transpose(1, 0, 2).copy(), cuda_device),
-                                            bits_to_torch(v.transpose(1, 0, 2).copy(), cuda_device), plan))[0]
+    out2 = gqa.decode_batch(bits_to_torch(np.stack([q, q]), cuda_device),
+                            bits_to_torch(k.transpose(1, 0, 2).copy(), cuda_device),
+                            bits_to_torch(v.transpose(1, 0, 2).copy(), cuda_device), plan)
+    merged = torch_to_bits(out2)[0]
+    np.testing.assert_array_equal(torch_to_bits(out2)[1], merged)
     assert check_rows(merged, clustered, 2).passed
     golden = gqa_golden(q, k, v, seq_len, qpos, exact=seq_len <= 1024)
     assert_parity(golden, clustered)
