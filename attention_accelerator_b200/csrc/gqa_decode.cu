@@ -7,10 +7,12 @@
 // (a "split").  This is the reference's per-KV-head group loop
 // (gqa_controller.v:140-277: Q group -> K position -> block) with the key loop
 // cut into splits so that every SM streams K/V rows at once.
-//   warp 8      producer: one thread issues a TMA tensor copy per 64-key K tile
-//               and V tile (16 KB each, one head, any K/V strides) into a
-//               4-stage shared-memory ring, one mbarrier per stage and direction.
-//   warps 0..7  consumers: warp c owns keys [8c, 8c+8) of every tile, four at a
+//   warp 11     producer: works out the CTA's (sequence, split), then one thread
+//               issues the group's 4 Q rows and, per 88-key tile, one TMA tensor
+//               copy for K and one for V (22 KB each, one head, any K/V strides)
+//               into a 4-stage shared-memory ring, one mbarrier per stage and
+//               direction.
+//   warps 0..10 consumers: warp c owns keys [8c, 8c+8) of every tile, four at a
 //               time: 8 lanes per key, each lane 8 rotate_half pairs (16 of the
 //               128 dims).  Per key: RoPE of K (rope_unit.v), the 4 Q.K dot
 //               products in FP32 (bf16_dot_product_mac.v + scale_unit.v), a
@@ -18,10 +20,14 @@
 //               (flash_softmax.v:233-490) and the P.V accumulation
 //               (output_accumulator.v:244-536) with each lane owning 4 dims.
 //               The P.V of tile t-1 is interleaved with the Q.K of tile t.
-//   epilogue    the 8 warps' (m, l, acc) merge through shared memory; a sequence
+//   epilogue    the 11 warps' (m, l, acc) merge through shared memory; a sequence
 //               with one split writes its BF16 rows (O * 1/l,
-//               output_accumulator.v:546-687) directly, otherwise each split
-//               writes an FP32 partial to the workspace for split_merge_kernel.
+//               output_accumulator.v:546-687) directly.  Otherwise each split
+//               writes an FP32 partial: for a batch, split_merge_kernel merges
+//               them; for a single sequence the last split of each KV head to
+//               finish merges them (arrival counter in the workspace header),
+//               and with gqa_decode_exchange also swaps the merged rows with
+//               the other GPUs of a sequence split over NVLink peer memory.
 //   cluster     (single sequence of up to 16 splits) the splits of one KV head
 //               run as one thread-block cluster: each keeps its partial in
 //               shared memory and, after a cluster barrier, merges 32 of the
@@ -494,8 +500,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     allow_dependent_launch();
     grid_dependency_wait();
 
-    // ---- which (sequence, split) this CTA owns: prefix sum of splits per sequence
-    if (warp == 0) {
+    // ---- which (sequence, split) this CTA owns: prefix sum of splits per sequence,
+    // computed by the producer warp, which goes on to issue the loads at once;
+    // the consumers pick the result up through named barrier 2.
+    if (warp == kConsumerWarps) {
         int b = 0, split = gsplit;
         if (!single) {
             int base = 0;
@@ -524,8 +532,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             info[0] = b;
             info[1] = split;
         }
+        __syncwarp();
+        named_barrier_arrive(2, kThreads);
+    } else {
+        named_barrier_sync(2, kThreads);
     }
-    __syncthreads();
     const int b = info[0];
     const int split = info[1];
     if (b < 0) return;  // grid larger than the plan: nothing to do (uniform per CTA)
@@ -665,12 +676,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
         const float m_new = fmaxf(m_run, mx);
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = exp2f(m_run - m_use);
+        const float alpha = fast_exp2(m_run - m_use);
         float psum = 0.f;
         float pv[kSteps];
 #pragma unroll
         for (int step = 0; step < kSteps; ++step) {
-            pv[step] = exp2f(sc[step] - m_use);
+            pv[step] = fast_exp2(sc[step] - m_use);
             psum += pv[step];
         }
         l_run = l_run * alpha + psum;

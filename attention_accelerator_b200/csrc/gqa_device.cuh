@@ -225,6 +225,12 @@ __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Arrive on a named barrier without waiting (the producer side of a hand-off:
+// shared-memory writes before it are visible to the threads that bar.sync on it).
+__device__ __forceinline__ void named_barrier_arrive(int id, int threads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // Thread-block cluster barrier (release on arrive, acquire on wait) and loads
 // from another CTA's shared memory in the cluster.
 __device__ __forceinline__ void cluster_sync_all() {
@@ -274,6 +280,14 @@ __device__ __forceinline__ float4 lds128f(const void* p) {
 // Two BF16 codes in one 32-bit word -> (element 2j, element 2j+1) as float2.
 __device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
     return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+// 2^x for x <= 0 with one MUFU.EX2 (PTX ex2.approx.ftz: relative error below 2^-22,
+// results below 2^-126 flushed to zero, which only drops weights under 2^-126 of the row max).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // ---------------------------------------------------------------------------
