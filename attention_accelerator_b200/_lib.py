@@ -73,6 +73,7 @@ class GqaChunkParams(ctypes.Structure):
 CHUNKED_WORKSPACE_BYTES = 256
 PEER_HANDLE_BYTES = 64
 CHUNKED_MAX_QUERIES = 128
+MEM_MAX_ELEMENTS = 4096
 
 _P = ctypes.c_void_p
 _SIGNATURES = {
@@ -105,6 +106,11 @@ _SIGNATURES = {
     "gqa_rope_phase_rom": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, ctypes.c_double]),
     "gqa_rope_sincos_rom": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
     "gqa_read_status": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int)]),
+    "gqa_mem_decode_workspace_bytes": (ctypes.c_size_t, [ctypes.c_size_t]),
+    "gqa_mem_decode": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.c_int, _P, ctypes.c_uint64, _P, _P,
+                                      ctypes.c_size_t, _P]),
+    "gqa_mem_encode_bytes": (ctypes.c_size_t, [ctypes.c_uint64, ctypes.c_int]),
+    "gqa_mem_encode": (ctypes.c_int, [_P, ctypes.c_uint64, ctypes.c_int, _P, _P]),
 }
 
 _lock = threading.Lock()

@@ -39,6 +39,90 @@ def read_mem(path: Path, elements: int) -> np.ndarray:
     return parse_mem_text(Path(path).read_text(), elements)
 
 
+# ---------------------------------------------------------------------------
+# The same codec on the GPU (gqa_mem_decode / gqa_mem_encode): the text goes to
+# the device once and is parsed there, so large vector files (K and V at long
+# SEQ_LEN are hundreds of MB of hex) skip host-side parsing.
+# ---------------------------------------------------------------------------
+
+def _device(device):
+    import torch
+    if device is None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("the GPU .mem codec needs a CUDA device (there is no CPU path)")
+        return torch.device("cuda", torch.cuda.current_device())
+    return torch.device(device)
+
+
+def decode_mem(data, elements: int, device=None):
+    """``.mem`` text -> int16 tensor ``[rows, elements]`` of BF16 codes on the GPU.
+
+    ``data`` is ``bytes`` (copied to the device) or a uint8 CUDA tensor.  Lines
+    follow ``read_mem`` (gqa_reference.py:44-46 with unpack_bf16, :31-36): blank
+    and ``//`` lines are skipped, ``_`` is ignored and every other line must hold
+    exactly ``4 * elements`` hex digits, else ``ValueError`` names the line.
+    """
+    import torch
+    from . import _lib
+    lib = _lib.load()
+    if not 1 <= elements <= _lib.MEM_MAX_ELEMENTS:
+        raise ValueError(f"elements must be in [1, {_lib.MEM_MAX_ELEMENTS}]")
+    if isinstance(data, torch.Tensor):
+        text = data.reshape(-1)
+        dev = text.device
+        if text.dtype != torch.uint8 or dev.type != "cuda":
+            raise TypeError("a tensor argument must be uint8 on a CUDA device")
+        if text.data_ptr() % 16:
+            text = text.clone()
+    else:
+        dev = _device(device)
+        host = torch.frombuffer(bytearray(data), dtype=torch.uint8) if len(data) else torch.empty(0, dtype=torch.uint8)
+        text = host.to(dev)
+    n = text.numel()
+    max_rows = n // (4 * elements)
+    rows = torch.empty((max(max_rows, 1), elements), dtype=torch.int16, device=dev)
+    result = torch.empty(2, dtype=torch.int64, device=dev)  # struct gqa_mem_result
+    ws_bytes = lib.gqa_mem_decode_workspace_bytes(n)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        st = lib.gqa_mem_decode(text.data_ptr() if n else None, n, elements, rows.data_ptr(), max_rows,
+                                result.data_ptr(), ws.data_ptr(), ws_bytes, stream)
+    if st != _lib.GQA_OK:
+        raise RuntimeError(f"gqa_mem_decode: {_lib.status_string(st)}")
+    n_rows, bad = (int(x) for x in result.cpu())
+    if bad != -1:  # UINT64_MAX read as int64
+        line = int((text[:bad] == ord("\n")).sum()) + 1
+        raise ValueError(f"line {line}: expected {4 * elements} hex digits (and '_'), "
+                         f"surrounded by blanks only")
+    if n_rows > max_rows:
+        raise RuntimeError("gqa_mem_decode found more rows than the text can hold")
+    return rows[:n_rows]
+
+
+def encode_mem(rows, device=None) -> bytes:
+    """int16/uint16 codes ``[rows, elements]`` -> the text ``write_mem`` writes, encoded on the GPU."""
+    import torch
+    from . import _lib
+    lib = _lib.load()
+    if isinstance(rows, np.ndarray):
+        rows = torch.from_numpy(np.ascontiguousarray(rows, dtype=np.uint16).view(np.int16)).to(_device(device))
+    if rows.dim() != 2 or rows.dtype not in (torch.int16, torch.bfloat16) or rows.device.type != "cuda":
+        raise TypeError("rows must be a 2-D int16 or bfloat16 CUDA tensor")
+    rows = rows.contiguous()
+    n_rows, elements = rows.shape
+    nbytes = lib.gqa_mem_encode_bytes(n_rows, elements)
+    if n_rows and nbytes == 0:
+        raise ValueError(f"elements must be in [1, {_lib.MEM_MAX_ELEMENTS}]")
+    text = torch.empty(max(nbytes, 4), dtype=torch.uint8, device=rows.device)
+    with torch.cuda.device(rows.device):
+        stream = torch.cuda.current_stream(rows.device).cuda_stream
+        st = lib.gqa_mem_encode(rows.data_ptr(), n_rows, elements, text.data_ptr(), stream)
+    if st != _lib.GQA_OK:
+        raise RuntimeError(f"gqa_mem_encode: {_lib.status_string(st)}")
+    return text[:nbytes].cpu().numpy().tobytes()
+
+
 def write_mem(path: Path, rows: np.ndarray) -> None:
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)

@@ -316,6 +316,50 @@ int gqa_decode_exchange(const void *q, const void *k, const void *v, void *out, 
  */
 int gqa_read_status(void *workspace, void *stream, int *device_status);
 
+/* ---------------------------------------------------------------------------
+ * The ".mem" transport text on the GPU.  Replaces the reference's host codec
+ * pyfiles/gqa_reference.py:26-46 (pack_bf16, unpack_bf16, write_mem, read_mem)
+ * for the vectors of gen_gqa_wrapper_vectors.py:111-119.
+ *
+ * A line holds `elements` BF16 codes as 4*elements hex digits, element 0 in
+ * the rightmost 4.  Decoding follows read_mem: lines end at \n, \r, \r\n, \v,
+ * \f or \x1c-\x1e; blank lines and lines whose first non-blank characters are
+ * "//" are skipped; '_' is ignored; blanks (space, \t, \x1f) may surround the
+ * digits but not sit between them; any other byte, or a digit count other
+ * than 4*elements, makes the line malformed.
+ * ------------------------------------------------------------------------- */
+#define GQA_MEM_MAX_ELEMENTS 4096
+
+typedef struct gqa_mem_result {
+    uint64_t rows;       /* data lines found (valid or malformed) */
+    uint64_t bad_offset; /* byte offset of the first malformed line, UINT64_MAX if none */
+} gqa_mem_result;
+
+/* Scratch for gqa_mem_decode: 8 bytes per 16 KB of text. */
+size_t gqa_mem_decode_workspace_bytes(size_t text_bytes);
+
+/*
+ * Decode `text` (device memory, 16-byte aligned, text_bytes long) into `rows`
+ * (device, uint16 [max_rows][elements], 4-byte aligned).  Rows past max_rows
+ * are counted but not written.  `result` (device memory) receives the row
+ * count and the first malformed line; read it after the stream has passed
+ * this call: the decode is valid iff result.bad_offset == UINT64_MAX and
+ * result.rows <= max_rows.  Asynchronous on `stream`; three kernel launches.
+ */
+int gqa_mem_decode(const void *text, size_t text_bytes, int elements, void *rows, uint64_t max_rows,
+                   gqa_mem_result *result, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Bytes of text gqa_mem_encode writes: n_rows * (4*elements + 1). */
+size_t gqa_mem_encode_bytes(uint64_t n_rows, int elements);
+
+/*
+ * Encode `rows` (device, uint16 [n_rows][elements]) as write_mem's text:
+ * lowercase hex, element 0 rightmost, '\n' after every line (the trailing
+ * newline included).  `text` (device, 4-byte aligned) receives
+ * gqa_mem_encode_bytes(n_rows, elements) bytes.  Asynchronous on `stream`.
+ */
+int gqa_mem_encode(const void *rows, uint64_t n_rows, int elements, void *text, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
