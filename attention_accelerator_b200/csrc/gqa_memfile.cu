@@ -7,7 +7,16 @@
 // drops '_' and requires exactly 4 * elements hex digits per remaining line
 // (unpack_bf16, :31-36).
 //
-// Decode, three kernels over the text in device memory:
+// Decode, fast path: text written by write_mem (and most files) has R lines of
+// exactly 4*elements hex digits and '\n' (the last '\n' optional).  When the
+// byte count fits that shape, mem_regular_kernel stages whole lines of the text
+// in shared memory (16-byte loads), converts each element's 4 characters with
+// byte-parallel (SWAR) arithmetic and checks that every character is a hex
+// digit and every line ends in '\n'.  Any mismatch sets a flag in the
+// workspace, and the general path below runs; otherwise its kernels return at
+// once.  So the call never waits on the host.
+//
+// Decode, general path, three kernels over the text in device memory:
 //   A  count      each thread owns a 64-byte segment of the text (four 16-byte
 //                 loads) and every run of non-separator bytes that STARTS in it
 //                 (following the run into later segments when it is longer).
@@ -38,6 +47,8 @@ constexpr int kSegBytes = 64;
 constexpr int kMemThreads = 256;
 constexpr int kBlockBytes = kSegBytes * kMemThreads;  // 16 KB of text per block
 constexpr int kScanThreads = 1024;
+constexpr int kRegularBytes = 16384;  // text staged per block on the fast path
+constexpr int kWsFlagBytes = 16;      // workspace: u32 "irregular" flag, then the per-block row counts
 
 // Byte classes.  Separators end a line as str.splitlines does for ASCII text
 // (\n, \r, \r\n, \v, \f, \x1c-\x1e); blanks are what str.strip removes inside
@@ -169,7 +180,135 @@ struct MemDecodeArgs {
     uint64_t max_rows;
     uint64_t* block_rows;  // [blocks]  A: rows per block; B: exclusive offsets
     gqa_mem_result* result;
+    const uint32_t* irregular;  // set by the fast path: the general path must run
 };
+
+// ---------------------------------------------------------------------------
+// Fast path.
+// ---------------------------------------------------------------------------
+struct MemRegularArgs {
+    const uint8_t* text;
+    uint64_t n;
+    int elements;
+    uint64_t n_rows;       // R
+    int rows_per_block;    // whole lines staged per block
+    uint16_t* rows;
+    uint64_t max_rows;
+    gqa_mem_result* result;
+    uint32_t* irregular;
+    bool units8;           // elements % 8 == 0 and rows 16-byte aligned: 8 elements per thread step
+};
+
+// Byte-parallel checks on 4 ASCII characters (first one in the low byte).  For
+// bytes below 0x80, b >= lo iff b + (0x80 - lo) has bit 7 set, and b <= hi iff
+// b + (0x7f - hi) has bit 7 clear; no carry crosses a byte.
+__device__ __forceinline__ uint32_t in_range4(uint32_t w, uint32_t lo, uint32_t hi) {
+    return (w + 0x80808080u - lo) & ~(w + 0x7f7f7f7fu - hi) & 0x80808080u;
+}
+// 0x80 in every byte that is a hex digit (bytes >= 0x80 give 0 through `ascii`).
+__device__ __forceinline__ uint32_t hex_mask4(uint32_t w) {
+    const uint32_t ascii = ~w & 0x80808080u;
+    const uint32_t low = w & 0x7f7f7f7fu;
+    return ascii & (in_range4(low, 0x30303030u, 0x39393939u) | in_range4(low | 0x20202020u, 0x61616161u, 0x66666666u));
+}
+// The 4 characters' nibbles, two per byte: byte 0 = c0 c1, byte 2 = c2 c3.
+__device__ __forceinline__ uint32_t nibbles4(uint32_t w) {
+    const uint32_t v = (w & 0x0f0f0f0fu) + ((w >> 6) & 0x01010101u) * 9u;  // one nibble per byte
+    return ((v & 0x000f000fu) << 4) | ((v >> 8) & 0x000f000fu);
+}
+// Four characters -> their 16-bit value (c0 is the most significant digit).
+__device__ __forceinline__ uint32_t hex4(uint32_t w, bool& ok) {
+    ok = hex_mask4(w) == 0x80808080u;
+    return __byte_perm(nibbles4(w), 0u, 0x4402u);
+}
+
+__global__ void __launch_bounds__(kMemThreads) mem_regular_kernel(const __grid_constant__ MemRegularArgs a) {
+    __shared__ __align__(16) uint32_t sm[kRegularBytes / 4 + 8];
+    const uint64_t width = 4ull * a.elements + 1;
+    const uint64_t r0 = (uint64_t)blockIdx.x * a.rows_per_block;
+    const uint64_t r1 = min(a.n_rows, r0 + a.rows_per_block);
+    if (blockIdx.x == 0 && threadIdx.x == 0) a.result->rows = a.n_rows;
+    // Stage text bytes [r0*width, min(r1*width, n)) from the 16-byte boundary below.
+    const uint64_t start = r0 * width, end = min(r1 * width, a.n);
+    const uint64_t a0 = start & ~15ull;
+    const uint64_t vec_end = end & ~15ull;
+    uint8_t* sb = reinterpret_cast<uint8_t*>(sm);
+    for (uint64_t off = a0 + 16ull * threadIdx.x; off < vec_end; off += 16ull * kMemThreads)
+        *reinterpret_cast<uint4*>(sb + (off - a0)) = __ldg(reinterpret_cast<const uint4*>(a.text + off));
+    for (uint64_t off = max(vec_end, a0) + threadIdx.x; off < end; off += kMemThreads) sb[off - a0] = a.text[off];
+    __syncthreads();
+    bool ok = true;
+    if (a.units8) {
+        // Thread step: 8 elements e0..e0+7 of one row = 32 characters, elements
+        // e0+7 .. e0 in text order; one 16-byte store.
+        const int per_row = a.elements / 8;
+        const int units = (int)(r1 - r0) * per_row;
+        const int step_r = kMemThreads / per_row, step_g = kMemThreads % per_row;
+        int r = threadIdx.x / per_row, gi = threadIdx.x % per_row;
+        uint32_t valid = 0x80808080u;
+        for (int u = threadIdx.x; u < units; u += kMemThreads) {
+            const uint64_t row = r0 + r;
+            const int e0 = 8 * gi;
+            const uint32_t o = (uint32_t)(start - a0 + (uint64_t)r * width + 4u * (a.elements - 8 - e0));
+            const uint32_t* src = sm + (o >> 2);
+            const uint32_t sh = 8 * (o & 3);
+            uint32_t w[8];
+            uint32_t prev = src[0];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const uint32_t next = src[k + 1];
+                w[k] = __funnelshift_r(prev, next, sh);  // characters of element e0+7-k
+                prev = next;
+                valid &= hex_mask4(w[k]);
+            }
+            if (gi == 0) {  // the line's end: '\n', or the text's end after its last line
+                const uint64_t nl = row * width + width - 1;
+                if (nl < a.n && sb[o + 32] != '\n') valid = 0;
+            }
+            uint32_t x[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) x[k] = nibbles4(w[k]);
+            // out word i/2 = value(e0+i) | value(e0+i+1) << 16; value(e0+i) comes from w[7-i]
+            uint4 q;
+            q.x = __byte_perm(x[7], x[6], 0x4602u);
+            q.y = __byte_perm(x[5], x[4], 0x4602u);
+            q.z = __byte_perm(x[3], x[2], 0x4602u);
+            q.w = __byte_perm(x[1], x[0], 0x4602u);
+            if (row < a.max_rows) *reinterpret_cast<uint4*>(a.rows + row * a.elements + e0) = q;
+            gi += step_g;
+            r += step_r;
+            if (gi >= per_row) {
+                gi -= per_row;
+                ++r;
+            }
+        }
+        ok = valid == 0x80808080u;
+    }
+    const int count = a.units8 ? 0 : (int)(r1 - r0) * a.elements;
+    const int step_r = kMemThreads / a.elements, step_e = kMemThreads % a.elements;
+    int r = threadIdx.x / a.elements, e = threadIdx.x % a.elements;
+    for (int j = threadIdx.x; j < count; j += kMemThreads) {
+        const uint64_t row = r0 + r;
+        const uint32_t o = (uint32_t)(start - a0 + (uint64_t)r * width + 4u * (a.elements - 1 - e));
+        const uint32_t w = __funnelshift_r(sm[o >> 2], sm[(o >> 2) + 1], 8 * (o & 3));
+        bool hex;
+        const uint32_t val = hex4(w, hex);
+        ok &= hex;
+        if (e == 0) {  // the line's end: '\n', or the text's end after its last line
+            const uint64_t nl = row * width + width - 1;
+            if (nl < a.n) ok &= sb[o + 4] == '\n';
+        }
+        if (row < a.max_rows) a.rows[row * a.elements + e] = (uint16_t)val;
+        e += step_e;
+        r += step_r;
+        if (e >= a.elements) {
+            e -= a.elements;
+            ++r;
+        }
+    }
+    if (__syncthreads_or(!ok) && threadIdx.x == 0) atomicOr(a.irregular, 1u);
+}
+
 
 // Walks this thread's segment.  For every run that starts in it, calls
 // on_run(kind, start) after the run's last byte (which may lie in a later
@@ -232,25 +371,34 @@ __device__ __forceinline__ uint32_t block_sum(uint32_t v, uint32_t* sh) {
     return t;
 }
 
-__global__ void __launch_bounds__(kMemThreads) mem_count_kernel(const __grid_constant__ MemDecodeArgs a) {
+// The general kernels loop over the 16 KB chunks with a bounded grid, so that
+// after a successful fast path they cost one small launch each.
+__global__ void __launch_bounds__(kMemThreads) mem_count_kernel(const __grid_constant__ MemDecodeArgs a, uint64_t chunks) {
     __shared__ uint32_t sh[kMemThreads / 32];
-    const uint64_t seg = (uint64_t)blockIdx.x * kMemThreads + threadIdx.x;
-    uint32_t rows = 0;
-    uint64_t bad = ~0ull;
-    walk_segment<false>(a, seg, nullptr, [&](int kind, uint64_t start) -> uint16_t* {
-        if (kind != 0) ++rows;
-        if (kind == 2 && start < bad) bad = start;
-        return nullptr;
-    });
-    if (bad != ~0ull) atomicMin(reinterpret_cast<unsigned long long*>(&a.result->bad_offset), (unsigned long long)bad);
-    const uint32_t total = block_sum(rows, sh);
-    if (threadIdx.x == 0) a.block_rows[blockIdx.x] = total;
+    if (*a.irregular == 0) return;  // the fast path decoded the text
+    for (uint64_t chunk = blockIdx.x; chunk < chunks; chunk += gridDim.x) {
+        const uint64_t seg = chunk * kMemThreads + threadIdx.x;
+        uint32_t rows = 0;
+        uint64_t bad = ~0ull;
+        walk_segment<false>(a, seg, nullptr, [&](int kind, uint64_t start) -> uint16_t* {
+            if (kind != 0) ++rows;
+            if (kind == 2 && start < bad) bad = start;
+            return nullptr;
+        });
+        if (bad != ~0ull)
+            atomicMin(reinterpret_cast<unsigned long long*>(&a.result->bad_offset), (unsigned long long)bad);
+        const uint32_t total = block_sum(rows, sh);
+        if (threadIdx.x == 0) a.block_rows[chunk] = total;
+        __syncthreads();  // sh is reused by the next chunk
+    }
 }
 
 // Exclusive scan of the per-block row counts in one block; writes the total.
-__global__ void __launch_bounds__(kScanThreads) mem_scan_kernel(uint64_t* counts, uint64_t blocks, gqa_mem_result* res) {
+__global__ void __launch_bounds__(kScanThreads) mem_scan_kernel(uint64_t* counts, uint64_t blocks, gqa_mem_result* res,
+                                                                const uint32_t* irregular) {
     __shared__ uint64_t sh[kScanThreads / 32];
     __shared__ uint64_t carry;
+    if (*irregular == 0) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) carry = 0;
     __syncthreads();
@@ -284,9 +432,8 @@ __global__ void __launch_bounds__(kScanThreads) mem_scan_kernel(uint64_t* counts
     if (threadIdx.x == 0) res->rows = carry;
 }
 
-__global__ void __launch_bounds__(kMemThreads) mem_decode_kernel(const __grid_constant__ MemDecodeArgs a) {
-    __shared__ uint32_t sh[kMemThreads / 32];
-    const uint64_t seg = (uint64_t)blockIdx.x * kMemThreads + threadIdx.x;
+__device__ __forceinline__ void decode_chunk(const MemDecodeArgs& a, uint64_t chunk, uint32_t* sh) {
+    const uint64_t seg = chunk * kMemThreads + threadIdx.x;
     // Rows of this thread's runs (counted again: the walk is cheap next to a
     // scratch array of per-thread counts).
     uint32_t mine = 0;
@@ -307,7 +454,7 @@ __global__ void __launch_bounds__(kMemThreads) mem_decode_kernel(const __grid_co
     uint32_t before = x - mine;
     for (int i = 0; i < warp; ++i) before += sh[i];
     if (mine == 0) return;
-    uint64_t row = a.block_rows[blockIdx.x] + before;
+    uint64_t row = a.block_rows[chunk] + before;
     auto row_ptr = [&](uint64_t r) -> uint16_t* {  // null past the caller's rows
         return r < a.max_rows ? a.rows + r * (uint64_t)a.elements : nullptr;
     };
@@ -315,6 +462,15 @@ __global__ void __launch_bounds__(kMemThreads) mem_decode_kernel(const __grid_co
         if (kind != 0) ++row;
         return row_ptr(row);
     });
+}
+
+__global__ void __launch_bounds__(kMemThreads) mem_decode_kernel(const __grid_constant__ MemDecodeArgs a, uint64_t chunks) {
+    __shared__ uint32_t sh[kMemThreads / 32];
+    if (*a.irregular == 0) return;
+    for (uint64_t chunk = blockIdx.x; chunk < chunks; chunk += gridDim.x) {
+        decode_chunk(a, chunk, sh);
+        __syncthreads();  // sh is reused by the next chunk
+    }
 }
 
 struct MemEncodeArgs {
@@ -360,7 +516,7 @@ uint64_t decode_blocks(size_t text_bytes) { return (text_bytes + kBlockBytes - 1
 extern "C" {
 
 size_t gqa_mem_decode_workspace_bytes(size_t text_bytes) {
-    return (size_t)gqa::decode_blocks(text_bytes) * sizeof(uint64_t) + 16;
+    return (size_t)gqa::decode_blocks(text_bytes) * sizeof(uint64_t) + gqa::kWsFlagBytes;
 }
 
 int gqa_mem_decode(const void* text, size_t text_bytes, int elements, void* rows, uint64_t max_rows,
@@ -378,17 +534,45 @@ int gqa_mem_decode(const void* text, size_t text_bytes, int elements, void* rows
         cudaMemsetAsync(&result->bad_offset, 0xff, sizeof(result->bad_offset), s) != cudaSuccess)
         return GQA_ERR_CUDA;
     if (!blocks) return GQA_OK;
+    uint32_t* irregular = static_cast<uint32_t*>(workspace);
+    // The fast path applies when the length is R lines of 4*elements digits + '\n'
+    // (the final '\n' optional) and a line fits the staging buffer.
+    const uint64_t width = 4ull * elements + 1;
+    uint64_t n_rows = 0;
+    if (text_bytes % width == 0) n_rows = text_bytes / width;
+    else if ((text_bytes + 1) % width == 0) n_rows = (text_bytes + 1) / width;
+    const int rows_per_block = (int)((gqa::kRegularBytes - 16) / width);
+    const bool regular = n_rows > 0 && rows_per_block >= 1;
+    if (cudaMemsetAsync(irregular, regular ? 0 : 1, sizeof(uint32_t), s) != cudaSuccess) return GQA_ERR_CUDA;
+    if (regular) {
+        gqa::MemRegularArgs f;
+        f.text = static_cast<const uint8_t*>(text);
+        f.n = text_bytes;
+        f.elements = elements;
+        f.n_rows = n_rows;
+        f.rows_per_block = rows_per_block;
+        f.rows = static_cast<uint16_t*>(rows);
+        f.max_rows = max_rows;
+        f.result = result;
+        f.irregular = irregular;
+        f.units8 = (elements % 8 == 0) && (reinterpret_cast<uintptr_t>(rows) % 16 == 0);
+        const uint64_t fb = (n_rows + rows_per_block - 1) / rows_per_block;
+        if (fb > 0x7fffffffull) return GQA_ERR_BATCH;
+        gqa::mem_regular_kernel<<<(unsigned)fb, gqa::kMemThreads, 0, s>>>(f);
+    }
     gqa::MemDecodeArgs a;
     a.text = static_cast<const uint8_t*>(text);
     a.n = text_bytes;
     a.elements = elements;
     a.rows = static_cast<uint16_t*>(rows);
     a.max_rows = max_rows;
-    a.block_rows = static_cast<uint64_t*>(workspace);
+    a.block_rows = reinterpret_cast<uint64_t*>(static_cast<uint8_t*>(workspace) + gqa::kWsFlagBytes);
     a.result = result;
-    gqa::mem_count_kernel<<<(unsigned)blocks, gqa::kMemThreads, 0, s>>>(a);
-    gqa::mem_scan_kernel<<<1, gqa::kScanThreads, 0, s>>>(a.block_rows, blocks, result);
-    gqa::mem_decode_kernel<<<(unsigned)blocks, gqa::kMemThreads, 0, s>>>(a);
+    a.irregular = irregular;
+    const unsigned grid = (unsigned)std::min<uint64_t>(blocks, 148ull * 8);
+    gqa::mem_count_kernel<<<grid, gqa::kMemThreads, 0, s>>>(a, blocks);
+    gqa::mem_scan_kernel<<<1, gqa::kScanThreads, 0, s>>>(a.block_rows, blocks, result, irregular);
+    gqa::mem_decode_kernel<<<grid, gqa::kMemThreads, 0, s>>>(a, blocks);
     return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }
 

@@ -8,7 +8,8 @@ status is 0 and stdout contains ``PASS:`` (:59, :72).  This program keeps that
 contract with the B200 library in place of the XSim testbench:
 
 * reads ``gqa_{q,k,v,golden}.mem`` and ``gqa_config.txt`` from VECTORS_DIR
-  (run_gqa_wrapper_sim.tcl:13-27);
+  (run_gqa_wrapper_sim.tcl:13-27), parsing the hex text on the GPU
+  (``gqa_mem_decode``);
 * programs the registers as the testbench does (tb_gqa_attention_wrapper.sv:323-329),
   taking QUERY_POSITION and KV_BLOCK_LEN from the config, and the exact
   1/sqrt(128) scale of the golden;
@@ -39,7 +40,7 @@ def _fail(msg: str, code: int = 1) -> int:
 def main(argv: list[str] | None = None) -> int:
     from . import _lib
     from .api import GqaConfigError, make_params
-    from .memfile import compare_rows, read_config, read_mem, write_mem
+    from .memfile import compare_rows, decode_mem, encode_mem, read_config
 
     vectors = Path(os.environ.get("VECTORS_DIR") or "tests/data").resolve()
     build = Path(os.environ.get("SIM_BUILD_DIR") or "build/gqa_wrapper_sim").resolve()
@@ -76,23 +77,26 @@ def main(argv: list[str] | None = None) -> int:
     from .api import decode
     if not torch.cuda.is_available():
         return _fail("no CUDA device: the B200 library has no CPU path")
-    q = read_mem(vectors / "gqa_q.mem", 16).reshape(-1, 128)
-    k = read_mem(vectors / "gqa_k.mem", 16).reshape(8, -1, 128)
-    v = read_mem(vectors / "gqa_v.mem", 16).reshape(8, -1, 128)
-    golden = read_mem(vectors / "gqa_golden.mem", 128)
     dev = torch.device("cuda", torch.cuda.current_device())
 
-    def to_dev(a):
-        return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16).to(dev)
+    def load(name, elements):  # the .mem text is parsed on the GPU
+        try:
+            return decode_mem((vectors / name).read_bytes(), elements, dev)
+        except ValueError as exc:
+            raise SystemExit(_fail(f"{vectors / name}: {exc}"))
 
+    q = load("gqa_q.mem", 16).view(torch.bfloat16).reshape(-1, 128)
+    k = load("gqa_k.mem", 16).view(torch.bfloat16).reshape(8, -1, 128)
+    v = load("gqa_v.mem", 16).view(torch.bfloat16).reshape(8, -1, 128)
+    golden = load("gqa_golden.mem", 128).cpu().numpy().view(np.uint16)
     try:
-        out = decode(to_dev(q), to_dev(k), to_dev(v), seq_len=seq_len, query_position=qpos,
-                     kv_block_len=kv_block_len, layout="head_major")
+        out = decode(q, k, v, seq_len=seq_len, query_position=qpos, kv_block_len=kv_block_len, layout="head_major")
     except GqaConfigError as exc:
         print(f"FAIL: configuration rejected: {exc}")
         return 1
-    rows = out.view(torch.int16).cpu().numpy().astype(np.uint16)
-    write_mem(out_path, rows)
+    out_rows = out.view(torch.int16)
+    out_path.write_bytes(encode_mem(out_rows))  # the testbench's row format, encoded on the GPU
+    rows = out_rows.cpu().numpy().view(np.uint16)
     if golden.shape != rows.shape:
         print(f"FAIL: golden has {golden.shape[0]} rows, output has {rows.shape[0]}")
         return 1

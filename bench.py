@@ -445,7 +445,107 @@ class ChunkedDecode(Workload):
         return None
 
 
+MEM_METRIC = ".mem transport text decoded on the GPU: GB/s of text read + BF16 codes written"
+
+
+def mem_k_text_rows(seq_len: int = 131072):
+    """Rows of config 4's K transport file: head-major [8][seq_len][128] as 16-element beats."""
+    return 8 * seq_len * 128 // 16
+
+
+class MemCodec(Workload):
+    """Section-8(f) row 1: decode of the reference's K vector file (gqa_k.mem,
+    gen_gqa_wrapper_vectors.py:111-119) at config 4's length on the GPU: a 545 MB
+    hex text in HBM -> 8 x 131072 x 128 BF16 codes.  One step = gqa_mem_decode
+    (two memsets and 4 kernels); the text alone exceeds 2x L2."""
+
+    def __init__(self, device, rank, world, seq_len=131072, seed=20260805):
+        import torch
+        from attention_accelerator_b200 import _lib, memfile
+        self.torch, self.lib = torch, _lib.load()
+        self.name = f"memcodec_k_s{seq_len}"
+        self.metric, self.unit = MEM_METRIC, "GB/s"
+        self.dtype = "u8"
+        self.launches_per_step = 4  # fast-path kernel + the general path's three (which return at once)
+        self.qheads_per_step = 0
+        g = torch.Generator(device=device).manual_seed(seed + 7919 * rank)
+        n_rows = mem_k_text_rows(seq_len)
+        codes = torch.randn((n_rows, 16), generator=g, device=device).to(torch.bfloat16).view(torch.int16)
+        text_bytes = self.lib.gqa_mem_encode_bytes(n_rows, 16)
+        self.text = torch.empty(text_bytes, dtype=torch.uint8, device=device)
+        st = self.lib.gqa_mem_encode(codes.data_ptr(), n_rows, 16, self.text.data_ptr(),
+                                     torch.cuda.current_stream(device).cuda_stream)
+        assert st == 0, st
+        self.want = codes
+        self.rows = torch.empty_like(codes)
+        self.result = torch.empty(2, dtype=torch.int64, device=device)
+        self.ws_bytes = self.lib.gqa_mem_decode_workspace_bytes(text_bytes)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=device)
+        self.n_rows, self.seq_len = n_rows, seq_len
+        self.bytes_per_step = text_bytes + n_rows * 16 * 2
+        self.memfile = memfile
+
+    def launch(self, i):
+        st = self.lib.gqa_mem_decode(self.text.data_ptr(), self.text.numel(), 16, self.rows.data_ptr(), self.n_rows,
+                                     self.result.data_ptr(), self.ws.data_ptr(), self.ws_bytes,
+                                     self.torch.cuda.current_stream().cuda_stream)
+        assert st == 0, st
+
+    def check(self):
+        n, bad = (int(x) for x in self.result.cpu())
+        assert bad == -1 and n == self.n_rows and self.torch.equal(self.rows, self.want), "memcodec decode mismatch"
+
+    def config(self):
+        return {"workload": self.name, "file": "gqa_k.mem of config 4 (head-major [8][131072][128], 16 codes a line)",
+                "text_bytes": self.text.numel(), "rows": self.n_rows,
+                "l2": "text of 545 MB read once per step (more than 2x L2)", "parallelism": "single GPU"}
+
+    def e2e_inputs(self):
+        return [self.text.cpu().pin_memory()]
+
+    def e2e_step(self, host):
+        dev = self.rows.device
+        text = host[0].to(dev, non_blocking=True)
+        n = text.numel()
+        self.lib.gqa_mem_decode(text.data_ptr(), n, 16, self.rows.data_ptr(), self.n_rows, self.result.data_ptr(),
+                                self.ws.data_ptr(), self.ws_bytes, self.torch.cuda.current_stream().cuda_stream)
+        out = self.rows.cpu()
+        self.check()
+        return out
+
+    def oracle_inputs(self):
+        return None
+
+    def gpu_result_set0(self):
+        return None
+
+
+def mem_cpu_run(budget_s: float, lines: int = 65536):
+    """read_mem of the reference (restated in oracle/bf16.py) on a bounded sample of the same text."""
+    import tempfile
+    import numpy as np
+    from oracle.bf16 import mem_text, read_mem
+    rng = np.random.default_rng(20260805)
+    rows = rng.integers(0, 65536, size=(lines, 16), dtype=np.uint16)
+    text = mem_text(rows)
+    with tempfile.TemporaryDirectory() as d:
+        f = Path(d) / "gqa_k.mem"
+        f.write_text(text)
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            got = read_mem(f, 16)
+            reps += 1
+            dt = time.perf_counter() - t0
+            if dt >= budget_s or reps >= 20:
+                break
+    assert len(got) == lines
+    per = len(text) + lines * 16 * 2
+    return per * reps / dt / 1e9, f"{reps} x read_mem of a {len(text) / 1e6:.1f} MB sample ({lines} lines), {dt:.1f} s"
+
+
 def make_workload(name, device, rank, world, layout="position_major", chunk_batch=16, exchange="fused"):
+    if name == "memcodec":
+        return MemCodec(device, rank, world)
     if name == "config1":
         return SingleDecode(device, rank, 30, 29, uniform=True, layout=layout)
     if name == "config2":
@@ -555,6 +655,9 @@ def cpu_baseline(wl, budget_s=10.0):
     import numpy as np
     from oracle import check_rows
     from oracle.parallel import gqa_golden_parallel
+    if isinstance(wl, MemCodec):
+        value, sample = mem_cpu_run(budget_s)
+        return {"value": round(value, 5), "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample}
     if isinstance(wl, ChunkedDecode):
         reps, dt = chunked_cpu_run(budget_s, wl.S)
         per_seq = wl.bytes_per_step / wl.batch
@@ -606,6 +709,18 @@ def reference_arm(args, rank, world):
     import torch
     from concurrent.futures import ThreadPoolExecutor
     from oracle.parallel import gqa_golden_parallel
+    if args.workload == "memcodec":
+        mem_cpu_run(0.0, 4096)
+        value, sample = mem_cpu_run(150.0 / max(1, args.steps + args.warmup) * args.steps)
+        print(json.dumps({
+            "metric": MEM_METRIC, "value": round(value, 5), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic .mem text (seeded codes)", "impl": "reference",
+            "config": {"workload": "memcodec", "sample": sample},
+            "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 5), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
     if args.workload == "config5":
         n_keys = 8192
         chunked_cpu_run(0.0, n_keys)  # warm-up of one sequence
@@ -669,7 +784,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", choices=("config1", "config2", "config3", "config4", "config5"), default="config2")
+    ap.add_argument("--workload", choices=("config1", "config2", "config3", "config4", "config5", "memcodec"),
+                    default="config2")
     ap.add_argument("--layout", choices=("position_major", "head_major"), default="position_major")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
@@ -717,6 +833,8 @@ def main():
     per_gpu_bytes = wl.bytes_per_step if wl.scaling == "weak" else wl.bytes_per_step / world
     achieved = per_gpu_bytes / (ms_step * 1e-3) / 1e9
 
+    if hasattr(wl, "check"):
+        wl.check()  # the timed steps' output is the expected decode
     e2e_dt, h2d, d2h = e2e_run(torch, wl, args.e2e_steps, device)
     if dist_on:
         t = torch.tensor([e2e_dt], dtype=torch.float64, device=device)
@@ -749,17 +867,18 @@ def main():
                     "algorithmic_bytes_per_launch": per_gpu_bytes}
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": getattr(wl, "metric", METRIC), "value": round(value, 2), "unit": getattr(wl, "unit", UNIT), "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True,
-            "scaling": wl.scaling, "vs_baseline": None, "dtype": "bf16",
+            "scaling": wl.scaling, "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
             "data": "synthetic, seeded torch RNG (N(0,1) unless the workload says otherwise)",
             "config": dict(wl.config(), parallelism=(f"dp{world} (independent sequences per GPU)"
                                                      if wl.scaling == "weak" else wl.config().get("parallelism"))),
             "pct_of_peak_hbm": round(100 * achieved / peak, 2),
-            "query_heads_per_s": round(wl.qheads_per_step * scale / (ms_step * 1e-3), 1),
+            "query_heads_per_s": (round(wl.qheads_per_step * scale / (ms_step * 1e-3), 1)
+                                  if wl.qheads_per_step else None),
             "roofline": roofline,
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "e2e": {"value": round(e2e_value, 3), "unit": getattr(wl, "unit", UNIT), "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": args.e2e_steps},
             "gpu_launches": args.steps * wl.launches_per_step,
             "clocks": clocks,

@@ -141,3 +141,35 @@ def test_round_trip_long_context_k_file(cuda_device):
     assert text == host_encode(host)
     back = memfile.decode_mem(text, 16)
     assert torch.equal(back, dev_rows)
+
+
+@pytest.mark.parametrize("variant", ["plain", "upper", "no_final_newline", "comment_same_length", "cr_line_end",
+                                     "blank_padded_line", "short_line_long_line"])
+def test_fixed_width_shape_and_look_alikes(variant, cuda_device, tmp_path):
+    """Texts whose byte count fits R lines of 4*elements digits + '\\n' take the fast
+    path; the look-alikes among them (same length, other content) must fall back to
+    the general parser and still match read_mem."""
+    rng = np.random.default_rng(7)
+    rows = rng.integers(0, 65536, size=(40, 16), dtype=np.uint16)
+    lines = mem_text(rows).splitlines()
+    if variant == "upper":
+        lines = [ln.upper() for ln in lines]
+    elif variant == "comment_same_length":
+        lines[7] = "//" + "x" * 62
+    elif variant == "blank_padded_line":
+        lines[3] = "  " + lines[3][:62]
+        lines[4] = lines[4][:60] + "    "
+    elif variant == "short_line_long_line":
+        lines[9], lines[10] = lines[9][:60], lines[10] + lines[9][60:]
+    text = "\n".join(lines) + ("" if variant == "no_final_newline" else "\n")
+    if variant == "cr_line_end":
+        text = text.replace("\n", "\r", 1)
+    data = text.encode()
+    assert len(data) in (40 * 65, 40 * 65 - 1)
+    try:
+        want = _oracle_decode(data, 16, tmp_path)
+    except ValueError:
+        with pytest.raises(ValueError):
+            memfile.decode_mem(data, 16)
+        return
+    np.testing.assert_array_equal(_gpu(data, 16), want)
