@@ -30,8 +30,8 @@
 //                 digits left to right: digit k belongs to element
 //                 elements-1-k/4 (the line is validated in A), and writes the
 //                 row two elements per 32-bit store.
-// Encode: one thread per 4-byte word of the output text; each byte is a
-// function of its position (row, column) alone, so the stores are coalesced.
+// Encode: one thread per 16 bytes of the output text (one division places the
+// chunk, then the bytes follow by counting), written with one 16-byte store.
 #include "gqa_b200.h"
 #include "gqa_internal.h"
 
@@ -211,10 +211,11 @@ __device__ __forceinline__ uint32_t hex_mask4(uint32_t w) {
     const uint32_t low = w & 0x7f7f7f7fu;
     return ascii & (in_range4(low, 0x30303030u, 0x39393939u) | in_range4(low | 0x20202020u, 0x61616161u, 0x66666666u));
 }
-// The 4 characters' nibbles, two per byte: byte 0 = c0 c1, byte 2 = c2 c3.
+// The 4 characters' nibbles, two per byte: byte 0 = c0 c1, byte 2 = c2 c3
+// (bytes 1 and 3 hold leftovers that the byte permutes below never select).
 __device__ __forceinline__ uint32_t nibbles4(uint32_t w) {
     const uint32_t v = (w & 0x0f0f0f0fu) + ((w >> 6) & 0x01010101u) * 9u;  // one nibble per byte
-    return ((v & 0x000f000fu) << 4) | ((v >> 8) & 0x000f000fu);
+    return (v << 4) | (v >> 8);
 }
 // Four characters -> their 16-bit value (c0 is the most significant digit).
 __device__ __forceinline__ uint32_t hex4(uint32_t w, bool& ok) {
@@ -481,28 +482,42 @@ struct MemEncodeArgs {
     uint64_t n;  // text bytes = n_rows * (4 * elements + 1)
 };
 
-__device__ __forceinline__ uint32_t text_byte(const MemEncodeArgs& a, uint64_t pos) {
-    const uint64_t width = 4ull * a.elements + 1;
-    const uint64_t line = pos / width;
-    const int col = (int)(pos - line * width);
-    if (col == 4 * a.elements) return '\n';
-    const int e = a.elements - 1 - (col >> 2);
-    const uint32_t v = a.rows[line * (uint64_t)a.elements + e];
-    const uint32_t nib = (v >> (4 * (3 - (col & 3)))) & 0xfu;
-    return nib < 10 ? '0' + nib : 'a' + nib - 10;
-}
-
+// Encode: thread per 16 bytes of text.  One division places the chunk's first
+// byte at (line, col); the walk then advances col and wraps at the line end.
 __global__ void __launch_bounds__(kMemThreads) mem_encode_kernel(const __grid_constant__ MemEncodeArgs a) {
+    const uint32_t width = 4u * a.elements + 1;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    for (uint64_t wi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; wi * 4 < a.n; wi += stride) {
-        const uint64_t pos = wi * 4;
-        if (pos + 4 <= a.n) {
-            uint32_t v = 0;
+    for (uint64_t ci = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; ci * 16 < a.n; ci += stride) {
+        const uint64_t pos = ci * 16;
+        uint64_t line = pos / width;
+        uint32_t col = (uint32_t)(pos - line * width);
+        uint32_t out[4] = {0u, 0u, 0u, 0u};
+        uint32_t v = 0;
+        const int nb = a.n - pos < 16 ? (int)(a.n - pos) : 16;
 #pragma unroll
-            for (int b = 0; b < 4; ++b) v |= text_byte(a, pos + b) << (8 * b);
-            *reinterpret_cast<uint32_t*>(a.text + pos) = v;
+        for (int b = 0; b < 16; ++b) {
+            uint32_t c = 0;
+            if (b < nb) {
+                if (col == width - 1) {
+                    c = '\n';
+                } else {
+                    if ((col & 3) == 0 || b == 0) v = a.rows[line * a.elements + (a.elements - 1 - (col >> 2))];
+                    const uint32_t nib = (v >> (12 - 4 * (col & 3))) & 0xfu;
+                    c = nib + (nib < 10 ? '0' : 'a' - 10);
+                }
+                if (++col == width) {
+                    col = 0;
+                    ++line;
+                }
+            }
+            out[b >> 2] |= c << (8 * (b & 3));
+        }
+        if (nb == 16) {
+            *reinterpret_cast<uint4*>(a.text + pos) = make_uint4(out[0], out[1], out[2], out[3]);
         } else {
-            for (uint64_t p = pos; p < a.n; ++p) a.text[p] = (uint8_t)text_byte(a, p);
+#pragma unroll
+            for (int b = 0; b < 16; ++b)
+                if (b < nb) a.text[pos + b] = (uint8_t)(out[b >> 2] >> (8 * (b & 3)));
         }
     }
 }
@@ -585,15 +600,15 @@ int gqa_mem_encode(const void* rows, uint64_t n_rows, int elements, void* text, 
     if (elements < 1 || elements > GQA_MEM_MAX_ELEMENTS) return GQA_ERR_GEOMETRY;
     if (!n_rows) return GQA_OK;
     if (!rows || !text) return GQA_ERR_NULL_POINTER;
-    if ((reinterpret_cast<uintptr_t>(text) & 3u) || (reinterpret_cast<uintptr_t>(rows) & 1u)) return GQA_ERR_ALIGNMENT;
+    if ((reinterpret_cast<uintptr_t>(text) & 15u) || (reinterpret_cast<uintptr_t>(rows) & 1u)) return GQA_ERR_ALIGNMENT;
     gqa::MemEncodeArgs a;
     a.rows = static_cast<const uint16_t*>(rows);
     a.n_rows = n_rows;
     a.elements = elements;
     a.text = static_cast<uint8_t*>(text);
     a.n = gqa_mem_encode_bytes(n_rows, elements);
-    const uint64_t words = (a.n + 3) / 4;
-    const unsigned grid = (unsigned)std::min<uint64_t>((words + gqa::kMemThreads - 1) / gqa::kMemThreads, 148ull * 16);
+    const uint64_t chunks = (a.n + 15) / 16;
+    const unsigned grid = (unsigned)std::min<uint64_t>((chunks + gqa::kMemThreads - 1) / gqa::kMemThreads, 148ull * 16);
     gqa::mem_encode_kernel<<<grid, gqa::kMemThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
     return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
 }

@@ -114,7 +114,7 @@ def encode_mem(rows, device=None) -> bytes:
     nbytes = lib.gqa_mem_encode_bytes(n_rows, elements)
     if n_rows and nbytes == 0:
         raise ValueError(f"elements must be in [1, {_lib.MEM_MAX_ELEMENTS}]")
-    text = torch.empty(max(nbytes, 4), dtype=torch.uint8, device=rows.device)
+    text = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=rows.device)
     with torch.cuda.device(rows.device):
         stream = torch.cuda.current_stream(rows.device).cuda_stream
         st = lib.gqa_mem_encode(rows.data_ptr(), n_rows, elements, text.data_ptr(), stream)

@@ -355,7 +355,7 @@ size_t gqa_mem_encode_bytes(uint64_t n_rows, int elements);
 /*
  * Encode `rows` (device, uint16 [n_rows][elements]) as write_mem's text:
  * lowercase hex, element 0 rightmost, '\n' after every line (the trailing
- * newline included).  `text` (device, 4-byte aligned) receives
+ * newline included).  `text` (device, 16-byte aligned) receives
  * gqa_mem_encode_bytes(n_rows, elements) bytes.  Asynchronous on `stream`.
  */
 int gqa_mem_encode(const void *rows, uint64_t n_rows, int elements, void *text, void *stream);
