@@ -28,6 +28,7 @@ GQA_ERR_CUDA = 13
 GQA_ERR_DEVICE_TIMEOUT = 14
 GQA_ERR_UNSUPPORTED_DEVICE = 15
 GQA_ERR_ROPE_THETA = 16
+GQA_ERR_FLAGS = 17
 
 #: codes that describe a bad call configuration (the reference's config_error)
 CONFIG_ERRORS = {GQA_ERR_GEOMETRY, GQA_ERR_SEQ_LEN, GQA_ERR_N_KV_TILES, GQA_ERR_SCALE,
@@ -35,6 +36,7 @@ CONFIG_ERRORS = {GQA_ERR_GEOMETRY, GQA_ERR_SEQ_LEN, GQA_ERR_N_KV_TILES, GQA_ERR_
                  GQA_ERR_BATCH, GQA_ERR_KV_RANGE, GQA_ERR_ROPE_THETA}
 
 GQA_FLAG_PARTIAL_OUT = 0x1
+GQA_FLAG_K_ROTATED = 0x2
 PARTIAL_FLOATS = 132
 
 
@@ -106,6 +108,7 @@ _SIGNATURES = {
     "gqa_rope_phase_rom": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, ctypes.c_double]),
     "gqa_rope_sincos_rom": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
     "gqa_read_status": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int)]),
+    "gqa_rope_k_cache": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, _P]),
     "gqa_mem_decode_workspace_bytes": (ctypes.c_size_t, [ctypes.c_size_t]),
     "gqa_mem_decode": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.c_int, _P, ctypes.c_uint64, _P, _P,
                                       ctypes.c_size_t, _P]),

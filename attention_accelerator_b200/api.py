@@ -134,7 +134,7 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, seq_len: int | 
            layout: str = "position_major", rope_theta: float = ROPE_THETA,
            n_q_heads: int = N_Q_HEADS, n_kv_heads: int = N_KV_HEADS, head_dim: int = HEAD_DIM,
            tile_dim: int = TILE_DIM, out: torch.Tensor | None = None,
-           mask_out: torch.Tensor | None = None) -> torch.Tensor:
+           mask_out: torch.Tensor | None = None, k_rotated: bool = False) -> torch.Tensor:
     """Single-token GQA decode of one sequence; returns BF16 ``[32, 128]``.
 
     ``q``: BF16 ``[32, 128]``.  ``k``/``v``: BF16 ``[rows, 8, 128]`` (``layout=
@@ -143,6 +143,8 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, seq_len: int | 
     ``seq_len`` defaults to the stored rows, ``query_position`` to SEQ_LEN-1,
     ``n_kv_tiles`` to ceil(SEQ_LEN/KV_BLOCK_LEN).  ``mask_out`` (uint8, CUDA,
     >= N_KV_TILES*KV_BLOCK_LEN entries) receives the kernel's key_valid() decisions.
+    ``k_rotated``: the K rows were rotated when they were stored (:func:`rope_k_cache`);
+    only Q is rotated here (``GQA_FLAG_K_ROTATED``).
     """
     lib = _lib.load()
     if seq_len is None:
@@ -151,6 +153,8 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, seq_len: int | 
                     group_size=group_size, n_kv_tiles=n_kv_tiles, scale=scale, n_q_heads=n_q_heads,
                     n_kv_heads=n_kv_heads, head_dim=head_dim, tile_dim=tile_dim, rope_theta=rope_theta)
     _check(lib.gqa_validate(ctypes.byref(p)), "decode")
+    if k_rotated:
+        p.flags |= _lib.GQA_FLAG_K_ROTATED
     host_io = not q.is_cuda
     device = torch.device("cuda", torch.cuda.current_device()) if host_io else q.device
     if host_io:
@@ -302,17 +306,19 @@ def plan_batch(seq_lens, *, query_positions=None, kv_starts=None, pos_begin=None
 
 def decode_batch(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, plan: BatchPlan, *,
                  layout: str = "position_major", scale: float | None = None,
-                 rope_theta: float = ROPE_THETA, out: torch.Tensor | None = None) -> torch.Tensor:
+                 rope_theta: float = ROPE_THETA, out: torch.Tensor | None = None,
+                 k_rotated: bool = False) -> torch.Tensor:
     """Batched ragged decode: ``q`` BF16 ``[B, 32, 128]``; one token per sequence.
 
     Returns BF16 ``[B, 32, 128]``, or with ``plan.partial`` FP32 ``[B, 32, 132]``
     partial rows (acc[128], m, l, pad) for a later :func:`combine_partials`.
+    ``k_rotated`` as for :func:`decode`.
     """
     lib = _lib.load()
     if q.dim() != 3 or q.shape[0] != plan.batch:
         raise ValueError(f"q must be [B={plan.batch}, 32, 128]")
     p = make_params(seq_len=1, scale=scale, rope_theta=rope_theta)
-    p.flags = _lib.GQA_FLAG_PARTIAL_OUT if plan.partial else 0
+    p.flags = (_lib.GQA_FLAG_PARTIAL_OUT if plan.partial else 0) | (_lib.GQA_FLAG_K_ROTATED if k_rotated else 0)
     device = q.device
     p.k_pos_stride, p.k_head_stride, k_rows = _kv_strides(k, layout)
     p.v_pos_stride, p.v_head_stride, v_rows = _kv_strides(v, layout)
@@ -361,6 +367,29 @@ def rope_rows(x: torch.Tensor, positions: torch.Tensor, rope_theta: float = ROPE
     out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
     _check(lib.gqa_rope_rows(x.data_ptr(), positions.data_ptr(), out.data_ptr(), x.shape[0], rope_theta,
                              _stream_ptr(x.device)), "rope_rows")
+    return out
+
+
+def rope_k_cache(k: torch.Tensor, positions: torch.Tensor, *, layout: str = "position_major",
+                 rope_theta: float = ROPE_THETA, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Pre-rotated K cache: RoPE of BF16 K rows ``[n, 8, 128]`` (``position_major``) or
+    ``[8, n, 128]`` (``head_major``), position i turned by ``positions[i]``, to BF16 rows
+    of the same layout (``out=k`` rotates in place).  Decode the result with
+    ``k_rotated=True``.  This is the append-time half of the reference's per-call K
+    RoPE (gen_gqa_wrapper_vectors.py:122-124)."""
+    lib = _lib.load()
+    if k.dtype != torch.bfloat16 or k.dim() != 3 or not k.is_cuda:
+        raise ValueError("k must be a bfloat16 CUDA tensor [n, 8, 128] or [8, n, 128]")
+    pos_stride, head_stride, n = _kv_strides(k, layout)
+    positions = positions.to(device=k.device, dtype=torch.int32).contiguous()
+    if positions.numel() != n:
+        raise ValueError(f"{positions.numel()} positions for {n} stored rows")
+    if out is None:
+        out = torch.empty_like(k)
+    if out.shape != k.shape or out.stride() != k.stride() or out.dtype != torch.bfloat16:
+        raise ValueError("out must match k's shape, strides and dtype")
+    _check(lib.gqa_rope_k_cache(k.data_ptr(), out.data_ptr(), positions.data_ptr(), n, pos_stride, head_stride,
+                                rope_theta, _stream_ptr(k.device)), "rope_k_cache")
     return out
 
 

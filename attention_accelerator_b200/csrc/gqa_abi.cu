@@ -171,6 +171,7 @@ int check_geometry(const gqa_params* p) {
 }
 
 int check_layout(const void* q, const void* k, const void* v, const void* out, const gqa_params* p) {
+    if (p->flags & ~(GQA_FLAG_PARTIAL_OUT | GQA_FLAG_K_ROTATED)) return GQA_ERR_FLAGS;
     if (!q || !k || !v || !out) return GQA_ERR_NULL_POINTER;
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return GQA_ERR_ALIGNMENT;
     if (!stride_ok(p->q_batch_stride) || !stride_ok(p->q_head_stride) || !stride_ok(p->k_head_stride) ||
@@ -368,6 +369,7 @@ const char* gqa_status_string(int status) {
         case GQA_ERR_DEVICE_TIMEOUT: return "a bounded wait inside a kernel timed out";
         case GQA_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 GPU";
         case GQA_ERR_ROPE_THETA: return "invalid rope_theta, or more than 4 distinct rope_theta values on one device";
+        case GQA_ERR_FLAGS: return "gqa_params.flags holds a bit this entry point does not support";
         default: return "unknown status";
     }
 }
@@ -514,7 +516,7 @@ int gqa_decode_exchange(const void* q, const void* k, const void* v, void* out, 
     if (world < 2 || world > gqa::kMaxPeers || rank < 0 || rank >= world) return GQA_ERR_BATCH;
     int st = check_geometry(p);
     if (st != GQA_OK) return st;
-    if (p->flags != 0) return GQA_ERR_BATCH;  // the exchange writes the final BF16 rows
+    if (p->flags & ~GQA_FLAG_K_ROTATED) return GQA_ERR_BATCH;  // the exchange writes the final BF16 rows
     st = check_layout(q, k, v, out, p);
     if (st != GQA_OK) return st;
     const gqa::SeqDesc d = *reinterpret_cast<const gqa::SeqDesc*>(shard);
@@ -619,6 +621,26 @@ int gqa_rope_rows(const void* x, const int32_t* positions, float* out, int rows,
     uint64_t step[gqa::kPairs];
     rope_steps((double)rope_theta, step, nullptr, nullptr, 0);
     if (gqa::launch_rope_rows(x, positions, out, rows, step, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return GQA_ERR_CUDA;
+    return GQA_OK;
+}
+
+int gqa_rope_k_cache(const void* k, void* k_rot, const int32_t* positions, int n_positions, int64_t pos_stride,
+                     int64_t head_stride, float rope_theta, void* stream) {
+    if (!k || !k_rot || !positions) return GQA_ERR_NULL_POINTER;
+    if (n_positions < 0) return GQA_ERR_BATCH;
+    if (!aligned16(k) || !aligned16(k_rot) || !stride_ok(pos_stride) || !stride_ok(head_stride) || pos_stride == 0 ||
+        head_stride == 0)
+        return GQA_ERR_ALIGNMENT;
+    if (!(rope_theta > 0.f) || !std::isfinite(rope_theta)) return GQA_ERR_ROPE_THETA;
+    if (n_positions == 0) return GQA_OK;
+    int sms = 0;
+    const int st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    uint64_t step[gqa::kPairs];
+    rope_steps((double)rope_theta, step, nullptr, nullptr, 0);
+    if (gqa::launch_rope_k_cache(k, k_rot, positions, n_positions, pos_stride, head_stride, step,
+                                 static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return GQA_ERR_CUDA;
     return GQA_OK;
 }

@@ -37,6 +37,7 @@
 // Both kernels are launched with programmatic dependent launch: everything that
 // reads only the argument block (barrier set-up, RoPE tables) runs before
 // griddepcontrol.wait, overlapping the tail of the previous kernel in the stream.
+#include "gqa_b200.h"
 #include "gqa_device.cuh"
 #include "gqa_internal.h"
 
@@ -438,6 +439,9 @@ static_assert((kConsumerWarps * kGroup * kPartialFloats + kGroup * kPartialFloat
                2 * kConsumerWarps * kGroup + kGroup + kGroup * kPartialFloats) * 4 <= kOffBars,
               "epilogue buffers fit the ring");
 
+// kKRotated: the K rows are stored already rotated (GQA_FLAG_K_ROTATED, RoPE
+// applied when they were appended); only Q is rotated here.
+template <bool kKRotated>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
@@ -480,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     // table (L2-resident after the first CTA); the two position-dependent rows
     // are computed exactly, one factor per thread of the first 128.
     float2 qfr[4], qfi[4], wr[4], wi[4], sr[4], si[4], tr[4], ti[4], lr[4], li[4];
-    if (warp < kConsumerWarps) {
+    if (!kKRotated && warp < kConsumerWarps) {
         rope_row8(rt->rot_step, g, sr, si);
         rope_row8(rt->rot_tile, g, tr, ti);
         rope_row8(rt->lane_off[c * 4 + slot], g, lr, li);
@@ -490,6 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             rope[tid] = rope_factor(rt->step[tid & (kPairs - 1)], tid < kPairs ? (int64_t)qpos : first_pos);
         named_barrier_sync(1, kConsumerThreads);
         rope_row8(rope + kRopeQ * kPairs, g, qfr, qfi);
+        if (kKRotated) return;
         float2 br[4], bi[4];
         rope_row8(rope + kRopeBase * kPairs, g, br, bi);
 #pragma unroll
@@ -616,6 +621,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             const int r = c * kKeysPerWarp + step * 4 + slot;
             const uint4 kre = *reinterpret_cast<const uint4*>(kt + r * kRowBytes + g * 16);
             const uint4 kim = *reinterpret_cast<const uint4*>(kt + r * kRowBytes + 128 + g * 16);
+            const uint32_t xw[4] = {kre.x, kre.y, kre.z, kre.w};
+            const uint32_t yw[4] = {kim.x, kim.y, kim.z, kim.w};
+            float2 rr[4], ri[4];
+            if constexpr (kKRotated) {
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    rr[jj] = bf16x2_to_float2(xw[jj]);
+                    ri[jj] = bf16x2_to_float2(yw[jj]);
+                }
+            } else {
             float2 ur[4], ui[4];
             if (step == 0) {
 #pragma unroll
@@ -627,12 +642,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) cmul2(wr[jj], wi[jj], sr[jj], si[jj], ur[jj], ui[jj]);
             }
-            const uint32_t xw[4] = {kre.x, kre.y, kre.z, kre.w};
-            const uint32_t yw[4] = {kim.x, kim.y, kim.z, kim.w};
-            float2 rr[4], ri[4];
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj)
                 cmul2(bf16x2_to_float2(xw[jj]), bf16x2_to_float2(yw[jj]), ur[jj], ui[jj], rr[jj], ri[jj]);
+            }
             float s[kGroup];
 #pragma unroll
             for (int hq = 0; hq < kGroup; ++hq) {
@@ -654,7 +667,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             sc[step] = r < rows ? u : -INFINITY;
         }
         // Advance the lane's RoPE factors by one tile (exactly every kReanchorTiles).
-        if (((t + 1) % kReanchorTiles) == 0) {
+        if (kKRotated) {
+            // no K factors
+        } else if (((t + 1) % kReanchorTiles) == 0) {
             rope_exact8(rt, g, first_pos + (int64_t)(t + 1) * kTileKeys + c * kKeysPerWarp + slot, wr, wi);
         } else {
 #pragma unroll
@@ -949,6 +964,30 @@ __global__ void __launch_bounds__(256) rope_rows_kernel(const __nv_bfloat16* __r
     }
 }
 
+// Pre-rotated K cache: one warp per (position, KV head) row, lane l owns pairs
+// 2l and 2l+1 (elements i, i+64), exact factors per element, BF16 out (RNE).
+// In place is safe: every element is read and written by the same lane.
+__global__ void __launch_bounds__(256) rope_k_cache_kernel(const __nv_bfloat16* k, __nv_bfloat16* out,
+                                                           const int32_t* __restrict__ pos, int rows,
+                                                           int64_t pos_stride, int64_t head_stride,
+                                                           const __grid_constant__ RopeSteps steps) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int i_pos = row / kNumKVHeads, h = row % kNumKVHeads;
+    const int64_t p = pos[i_pos];
+    const int64_t off = (int64_t)i_pos * pos_stride + (int64_t)h * head_stride;
+    const int i = 2 * lane;
+    const __nv_bfloat162 x2 = *reinterpret_cast<const __nv_bfloat162*>(k + off + i);
+    const __nv_bfloat162 y2 = *reinterpret_cast<const __nv_bfloat162*>(k + off + i + kPairs);
+    const float2 xv = __bfloat1622float2(x2), yv = __bfloat1622float2(y2);
+    const float2 f0 = rope_factor(steps.step[i], p), f1 = rope_factor(steps.step[i + 1], p);
+    const float re0 = fmaf(xv.x, f0.x, -(yv.x * f0.y)), im0 = fmaf(xv.x, f0.y, yv.x * f0.x);
+    const float re1 = fmaf(xv.y, f1.x, -(yv.y * f1.y)), im1 = fmaf(xv.y, f1.y, yv.y * f1.x);
+    *reinterpret_cast<__nv_bfloat162*>(out + off + i) = __floats2bfloat162_rn(re0, re1);
+    *reinterpret_cast<__nv_bfloat162*>(out + off + i + kPairs) = __floats2bfloat162_rn(im0, im1);
+}
+
 // Launch with programmatic dependent launch and, for cluster_x > 0, thread-block
 // clusters of (cluster_x, 1, 1).
 cudaError_t launch_pdl(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, void** args,
@@ -1044,11 +1083,14 @@ int decode_last_merge_max_splits() { return kLastMergeMaxSplits; }
 
 cudaError_t decode_prepare(int device) {
     (void)device;
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    // Clusters of up to 16 CTAs (above 8 is opt-in); without it clusters stay off.
-    if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-        (void)cudaGetLastError();
+    for (const void* f : {reinterpret_cast<const void*>(decode_kernel<false>),
+                          reinterpret_cast<const void*>(decode_kernel<true>)}) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
+        // Clusters of up to 16 CTAs (above 8 is opt-in); without it clusters stay off.
+        if (cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+            (void)cudaGetLastError();
+    }
     return cudaSuccess;
 }
 
@@ -1066,7 +1108,7 @@ int decode_cluster_capacity(int cluster) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, decode_kernel, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, decode_kernel<false>, &cfg) != cudaSuccess) {
         (void)cudaGetLastError();
         return 0;
     }
@@ -1075,11 +1117,11 @@ int decode_cluster_capacity(int cluster) {
 
 cudaError_t launch_decode(const DecodeArgs& a, int total_splits, cudaStream_t stream) {
     void* dargs[] = {const_cast<DecodeArgs*>(&a)};
+    const void* kern = (a.flags & GQA_FLAG_K_ROTATED) ? reinterpret_cast<const void*>(decode_kernel<true>)
+                                                       : reinterpret_cast<const void*>(decode_kernel<false>);
     if (a.cluster > 0)  // single sequence, merged inside the clusters
-        return launch_pdl(reinterpret_cast<const void*>(decode_kernel), dim3(a.cluster, kNumKVHeads), dim3(kThreads),
-                          kSmemBytes, stream, dargs, a.cluster);
-    cudaError_t e = launch_pdl(reinterpret_cast<const void*>(decode_kernel), dim3(total_splits * kNumKVHeads),
-                               dim3(kThreads), kSmemBytes, stream, dargs);
+        return launch_pdl(kern, dim3(a.cluster, kNumKVHeads), dim3(kThreads), kSmemBytes, stream, dargs, a.cluster);
+    cudaError_t e = launch_pdl(kern, dim3(total_splits * kNumKVHeads), dim3(kThreads), kSmemBytes, stream, dargs);
     // Done when every sequence had one split or the last split of each head merged.
     if (e != cudaSuccess || total_splits <= a.batch || a.ws_arrivals != nullptr) return e;
     MergeArgs m;
@@ -1106,6 +1148,18 @@ cudaError_t launch_rope_rows(const void* x, const int32_t* pos, float* out, int 
     RopeSteps s;
     for (int i = 0; i < kPairs; ++i) s.step[i] = step[i];
     rope_rows_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), pos, out, rows, s);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_k_cache(const void* k, void* out, const int32_t* pos, int n_positions, int64_t pos_stride,
+                                int64_t head_stride, const uint64_t* step, cudaStream_t stream) {
+    RopeSteps s;
+    for (int i = 0; i < kPairs; ++i) s.step[i] = step[i];
+    const int64_t rows = (int64_t)n_positions * kNumKVHeads;
+    if (rows > 0x7fffffffLL) return cudaErrorInvalidValue;
+    rope_k_cache_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(k), static_cast<__nv_bfloat16*>(out), pos, (int)rows, pos_stride,
+        head_stride, s);
     return cudaGetLastError();
 }
 

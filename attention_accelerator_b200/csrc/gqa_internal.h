@@ -33,6 +33,8 @@ int decode_cluster_capacity(int cluster);
 cudaError_t launch_decode(const DecodeArgs& a, int total_splits, cudaStream_t stream);
 cudaError_t launch_combine(const float* parts, int n_parts, int64_t part_stride, int64_t batch_stride, int batch,
                            void* out, int64_t o_bstride, int64_t o_hstride, cudaStream_t stream);
+cudaError_t launch_rope_k_cache(const void* k, void* out, const int32_t* pos, int n_positions, int64_t pos_stride,
+                                int64_t head_stride, const uint64_t* step, cudaStream_t stream);
 cudaError_t launch_rope_rows(const void* x, const int32_t* pos, float* out, int rows, const uint64_t* step,
                              cudaStream_t stream);
 

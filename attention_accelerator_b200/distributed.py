@@ -122,7 +122,7 @@ class PeerExchange:
 
     def decode(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, plan, *, layout: str = "position_major",
                scale: float | None = None, rope_theta: float | None = None,
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None, k_rotated: bool = False) -> torch.Tensor:
         """Decode this rank's shard of one sequence and exchange inside the same kernel.
 
         ``plan``: :func:`attention_accelerator_b200.plan_batch` of one sequence with
@@ -135,6 +135,8 @@ class PeerExchange:
         if self.batch != 1 or plan.batch != 1 or plan.partial:
             raise ValueError("decode() exchanges one sequence: PeerExchange(1) and a plan of one, partial=False")
         p = api.make_params(seq_len=1, scale=scale, rope_theta=api.ROPE_THETA if rope_theta is None else rope_theta)
+        if k_rotated:  # pre-rotated K cache (api.rope_k_cache)
+            p.flags |= _lib.GQA_FLAG_K_ROTATED
         p.k_pos_stride, p.k_head_stride, _ = api._kv_strides(k, layout)
         p.v_pos_stride, p.v_head_stride, _ = api._kv_strides(v, layout)
         if out is None:

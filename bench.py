@@ -125,6 +125,7 @@ class ClockSampler:
 class Workload:
     name = ""
     scaling = "weak"
+    k_rotated = False  # --k-rotated: K stored pre-rotated (GQA_FLAG_K_ROTATED), only Q rotated per call
     launches_per_step = 1
     graph_ok = False  # multi-launch steps under torch.distributed: graphs only without collectives
 
@@ -178,7 +179,7 @@ class SingleDecode(Workload):
     def launch(self, i):
         j = i % self.nsets
         self.gqa.decode(self.q[j], self.k[j], self.v[j], seq_len=self.S, query_position=self.qpos, out=self.out,
-                        layout=self.layout)
+                        layout=self.layout, k_rotated=self.k_rotated)
 
     def config(self):
         lay = "position_major [S,8,128]" if self.layout == "position_major" else "head_major [8,S,128]"
@@ -195,7 +196,8 @@ class SingleDecode(Workload):
 
     def e2e_step(self, host):
         q, k, v = host
-        return self.gqa.decode(q, k, v, seq_len=self.S, query_position=self.qpos, layout=self.layout)
+        return self.gqa.decode(q, k, v, seq_len=self.S, query_position=self.qpos, layout=self.layout,
+                               k_rotated=self.k_rotated)
 
     def oracle_inputs(self):
         """Head-major BF16 codes of buffer set 0 for the CPU restatement."""
@@ -211,6 +213,8 @@ class SingleDecode(Workload):
 
     def gpu_result_set0(self):
         import numpy as np
+        if self.k_rotated:  # the oracle port below rotates K per call
+            return None
         self.launch(0)
         self.torch.cuda.synchronize()
         return self.out.view(self.torch.int16).cpu().numpy().astype(np.uint16)
@@ -251,7 +255,7 @@ class RaggedBatch(Workload):
 
     def launch(self, i):
         j = i % self.nsets
-        self.gqa.decode_batch(self.q[j], self.k[j], self.v[j], self.plan, out=self.out)
+        self.gqa.decode_batch(self.q[j], self.k[j], self.v[j], self.plan, out=self.out, k_rotated=self.k_rotated)
 
     def config(self):
         return {"workload": self.name, "batch_per_gpu": self.batch, "seq_len": "U{512..8192} seeded",
@@ -265,7 +269,7 @@ class RaggedBatch(Workload):
         t = self.torch
         dev = self.out.device
         q, k, v = (x.to(dev, non_blocking=True) for x in host)
-        out = self.gqa.decode_batch(q, k, v, self.plan)
+        out = self.gqa.decode_batch(q, k, v, self.plan, k_rotated=self.k_rotated)
         return out.cpu()
 
     def oracle_inputs(self):
@@ -326,15 +330,16 @@ class LongContext(Workload):
 
     def launch(self, i):
         j = i % self.nsets
+        kr = self.k_rotated
         if self.world == 1:
             self.gqa.decode(self.q[j][0], self.k[j], self.v[j], seq_len=self.S, query_position=self.S - 1,
-                            out=self.out)
+                            out=self.out, k_rotated=kr)
             return
         import torch.distributed as dist
         if self.exchange == "fused":
-            self.peer.decode(self.q[j], self.k[j], self.v[j], self.plan, out=self.out)
+            self.peer.decode(self.q[j], self.k[j], self.v[j], self.plan, out=self.out, k_rotated=kr)
             return
-        self.gqa.decode_batch(self.q[j], self.k[j], self.v[j], self.plan, out=self.part)
+        self.gqa.decode_batch(self.q[j], self.k[j], self.v[j], self.plan, out=self.part, k_rotated=kr)
         if self.exchange == "peer":
             self.peer.combine(self.part, out=self.out)  # NVLink peer exchange fused with the LSE combine
             return
@@ -358,15 +363,16 @@ class LongContext(Workload):
     def e2e_step(self, host):
         dev = self.device
         q, k, v = (x.to(dev, non_blocking=True) for x in host)
+        kr = self.k_rotated
         if self.world == 1:
-            out = self.gqa.decode(q[0], k, v, seq_len=self.S, query_position=self.S - 1)
+            out = self.gqa.decode(q[0], k, v, seq_len=self.S, query_position=self.S - 1, k_rotated=kr)
         elif self.exchange == "fused":
-            out = self.peer.decode(q, k, v, self.plan)
+            out = self.peer.decode(q, k, v, self.plan, k_rotated=kr)
         elif self.exchange == "peer":
-            out = self.peer.combine(self.gqa.decode_batch(q, k, v, self.plan))
+            out = self.peer.combine(self.gqa.decode_batch(q, k, v, self.plan, k_rotated=kr))
         else:
             from attention_accelerator_b200.distributed import gather_partials
-            part = self.gqa.decode_batch(q, k, v, self.plan)
+            part = self.gqa.decode_batch(q, k, v, self.plan, k_rotated=kr)
             out = self.gqa.combine_partials(gather_partials(part))
         return out.cpu()
 
@@ -793,6 +799,8 @@ def main():
     ap.add_argument("--exchange", choices=("fused", "peer", "nccl"), default="fused",
                     help="config4 at N>1: exchange inside the decode kernel (fused), in a separate combine kernel "
                          "over peer memory (peer), or NCCL all-gather + combine (nccl)")
+    ap.add_argument("--k-rotated", action="store_true",
+                    help="configs 1-4: K cache stored pre-rotated (GQA_FLAG_K_ROTATED); decode rotates only Q")
     ap.add_argument("--chunk-batch", type=int, default=16,
                     help="config5 sequences (16 is the BASELINE config; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -817,6 +825,10 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
         build_library()
     wl = make_workload(args.workload, device, rank, world, args.layout, args.chunk_batch, args.exchange)
+    if args.k_rotated:
+        if args.workload not in ("config1", "config2", "config3", "config4"):
+            raise SystemExit("--k-rotated applies to the decode workloads config1-4")
+        wl.k_rotated = True
     stream = torch.cuda.Stream(device)
     sampler = ClockSampler(local) if rank == 0 else None
     ms, window = timed_graph_run(torch, wl, args.steps, args.warmup, stream, dist_on)
@@ -871,7 +883,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True,
             "scaling": wl.scaling, "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
             "data": "synthetic, seeded torch RNG (N(0,1) unless the workload says otherwise)",
-            "config": dict(wl.config(), parallelism=(f"dp{world} (independent sequences per GPU)"
+            "config": dict(wl.config(), **({"k_cache": "pre-rotated at append time (GQA_FLAG_K_ROTATED)"}
+                                              if wl.k_rotated else {}), parallelism=(f"dp{world} (independent sequences per GPU)"
                                                      if wl.scaling == "weak" else wl.config().get("parallelism"))),
             "pct_of_peak_hbm": round(100 * achieved / peak, 2),
             "query_heads_per_s": (round(wl.qheads_per_step * scale / (ms_step * 1e-3), 1)

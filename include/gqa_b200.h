@@ -50,11 +50,19 @@ enum gqa_status {
     GQA_ERR_CUDA = 13,             /* a CUDA runtime call (launch, attribute, copy) failed */
     GQA_ERR_DEVICE_TIMEOUT = 14,   /* a bounded wait inside a kernel gave up (see gqa_read_status) */
     GQA_ERR_UNSUPPORTED_DEVICE = 15, /* current device is not sm_100 */
-    GQA_ERR_ROPE_THETA = 16        /* rope_theta <= 0, not finite, or a 5th distinct value on one device */
+    GQA_ERR_ROPE_THETA = 16,       /* rope_theta <= 0, not finite, or a 5th distinct value on one device */
+    GQA_ERR_FLAGS = 17             /* gqa_params.flags holds a bit this entry point does not know */
 };
 
 /* GQA_FLAG_* values for gqa_params.flags. */
 #define GQA_FLAG_PARTIAL_OUT 0x1u  /* write FP32 partials (see gqa_partial_row) instead of BF16 rows */
+/* K rows are stored already rotated: RoPE was applied when each row was appended
+ * (gqa_rope_k_cache), so decode rotates only Q.  The production KV-cache
+ * convention; with it the reference's per-call RoPE of every K row
+ * (gen_gqa_wrapper_vectors.py:122-124, rope_unit.v) moves to append time.
+ * Accepted by gqa_decode, gqa_decode_batched, gqa_decode_noalloc and
+ * gqa_decode_exchange. */
+#define GQA_FLAG_K_ROTATED 0x2u
 
 /*
  * Call parameters.  The first block mirrors the reference's AXI-Lite register
@@ -259,6 +267,18 @@ int gqa_decode_chunked(const void *q, const void *k, const void *v, void *out, c
  */
 int gqa_rope_rows(const void *x, const int32_t *positions, float *out, int rows,
                   float rope_theta, void *stream);
+
+/*
+ * Pre-rotated K cache: RoPE of the K rows of `n_positions` positions, 8 KV
+ * heads each, written as BF16 (round to nearest even).  Row (i, h) is
+ * k + i*pos_stride + h*head_stride (elements) and turns by positions[i]
+ * (rope_half_split, gen_gqa_wrapper_vectors.py:25-35, with exact per-element
+ * factors).  k_rot has the same layout; k_rot == k rotates in place.  Decode
+ * such a cache with GQA_FLAG_K_ROTATED.  Pointers 16-byte aligned, strides
+ * multiples of 8.
+ */
+int gqa_rope_k_cache(const void *k, void *k_rot, const int32_t *positions, int n_positions,
+                     int64_t pos_stride, int64_t head_stride, float rope_theta, void *stream);
 
 /*
  * The RoPE ROM tables of tools/gen_rope_rom.py:41-57, computed on the host:

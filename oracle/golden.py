@@ -100,13 +100,15 @@ class _Neumaier:
 def gqa_golden_f64(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray,
                    seq_len: int, query_position: int, *, group: int = 4,
                    theta: float = ROPE_THETA, exact: bool = True,
-                   pos_chunk: int = 2048) -> np.ndarray:
+                   pos_chunk: int = 2048, k_rotated: bool = False) -> np.ndarray:
     """Float64 attention output ``[n_q_heads, D]`` before the final BF16 rounding.
 
     ``q_bits``: ``[n_q, D]`` BF16 codes; ``k_bits``/``v_bits``: ``[n_kv, >=seq_len, D]``
     BF16 codes in head-major order (gen_gqa_wrapper_vectors.py:85-107).
     Keys ``p`` in ``[0, query_position]`` contribute (:132-133); rows past that are
     never read, which is the pad/causal mask of :83 and :125-126.
+    ``k_rotated``: ``k_bits`` already hold rotated keys (a pre-rotated K cache), so
+    the per-key rope_half_split of :122-124 is skipped; Q is rotated as always.
     """
     if not 0 <= query_position < seq_len:
         raise ValueError("query_position must be in [0, seq_len)")
@@ -120,7 +122,8 @@ def gqa_golden_f64(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray,
     scores = np.empty((n_q, n_vis), dtype=np.float64)
     for p0 in range(0, n_vis, pos_chunk):
         p1 = min(n_vis, p0 + pos_chunk)
-        k_ref = rope_half_split(bf16_to_f32(k_bits[:, p0:p1]), np.arange(p0, p1), theta, exact)
+        k_ref = (bf16_to_f32(k_bits[:, p0:p1]) if k_rotated
+                 else rope_half_split(bf16_to_f32(k_bits[:, p0:p1]), np.arange(p0, p1), theta, exact))
         kq = k_ref[head_of]                                     # [n_q, n, D]
         if exact:
             prods = q_ref[:, None, :] * kq                      # per-element products, :132
