@@ -37,6 +37,7 @@ CONFIG_ERRORS = {GQA_ERR_GEOMETRY, GQA_ERR_SEQ_LEN, GQA_ERR_N_KV_TILES, GQA_ERR_
 
 GQA_FLAG_PARTIAL_OUT = 0x1
 GQA_FLAG_K_ROTATED = 0x2
+GQA_FLAG_Q_ROTATED = 0x4
 PARTIAL_FLOATS = 132
 
 
@@ -109,6 +110,8 @@ _SIGNATURES = {
     "gqa_rope_sincos_rom": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
     "gqa_read_status": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int)]),
     "gqa_rope_k_cache": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, _P]),
+    "gqa_rope_rtl": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _P, _P,
+                                    ctypes.c_int, _P]),
     "gqa_mem_decode_workspace_bytes": (ctypes.c_size_t, [ctypes.c_size_t]),
     "gqa_mem_decode": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.c_int, _P, ctypes.c_uint64, _P, _P,
                                       ctypes.c_size_t, _P]),

@@ -16,7 +16,7 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB = PKG / "lib" / "libgqa_b200.so"
 SOURCES = [CSRC / "gqa_abi.cu", CSRC / "gqa_decode.cu", CSRC / "gqa_noalloc.cu", CSRC / "gqa_chunked.cu", CSRC / "gqa_peer.cu",
-           CSRC / "gqa_memfile.cu"]
+           CSRC / "gqa_memfile.cu", CSRC / "gqa_rtl.cu"]
 HEADERS = [INCLUDE / "gqa_b200.h", CSRC / "gqa_device.cuh", CSRC / "gqa_internal.h"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

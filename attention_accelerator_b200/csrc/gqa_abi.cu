@@ -171,7 +171,7 @@ int check_geometry(const gqa_params* p) {
 }
 
 int check_layout(const void* q, const void* k, const void* v, const void* out, const gqa_params* p) {
-    if (p->flags & ~(GQA_FLAG_PARTIAL_OUT | GQA_FLAG_K_ROTATED)) return GQA_ERR_FLAGS;
+    if (p->flags & ~(GQA_FLAG_PARTIAL_OUT | GQA_FLAG_K_ROTATED | GQA_FLAG_Q_ROTATED)) return GQA_ERR_FLAGS;
     if (!q || !k || !v || !out) return GQA_ERR_NULL_POINTER;
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return GQA_ERR_ALIGNMENT;
     if (!stride_ok(p->q_batch_stride) || !stride_ok(p->q_head_stride) || !stride_ok(p->k_head_stride) ||
@@ -516,7 +516,7 @@ int gqa_decode_exchange(const void* q, const void* k, const void* v, void* out, 
     if (world < 2 || world > gqa::kMaxPeers || rank < 0 || rank >= world) return GQA_ERR_BATCH;
     int st = check_geometry(p);
     if (st != GQA_OK) return st;
-    if (p->flags & ~GQA_FLAG_K_ROTATED) return GQA_ERR_BATCH;  // the exchange writes the final BF16 rows
+    if (p->flags & ~(GQA_FLAG_K_ROTATED | GQA_FLAG_Q_ROTATED)) return GQA_ERR_BATCH;  // final BF16 rows only
     st = check_layout(q, k, v, out, p);
     if (st != GQA_OK) return st;
     const gqa::SeqDesc d = *reinterpret_cast<const gqa::SeqDesc*>(shard);

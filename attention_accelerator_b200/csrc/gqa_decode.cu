@@ -494,6 +494,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             rope[tid] = rope_factor(rt->step[tid & (kPairs - 1)], tid < kPairs ? (int64_t)qpos : first_pos);
         named_barrier_sync(1, kConsumerThreads);
         rope_row8(rope + kRopeQ * kPairs, g, qfr, qfi);
+        if (a.flags & GQA_FLAG_Q_ROTATED) {  // Q supplied rotated: identity factors (exact)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                qfr[jj] = make_float2(1.f, 1.f);
+                qfi[jj] = make_float2(0.f, 0.f);
+            }
+        }
         if (kKRotated) return;
         float2 br[4], bi[4];
         rope_row8(rope + kRopeBase * kPairs, g, br, bi);

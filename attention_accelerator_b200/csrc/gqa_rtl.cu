@@ -1,0 +1,75 @@
+// gqa_rtl.cu -- RTL-numerics RoPE: rows rotated the way the reference RTL
+// rotates them (rope_unit.v), so that decode outputs can be compared with a
+// dump of the RTL datapath.
+//
+//   phase = (phase_rom[i] * pos) mod 2^32           NCO, rope_unit.v:159-172
+//   addr  = phase >> (32 - rom_addr_bits)           top ROM_ADDR_BITS bits (14)
+//   {cos, sin} = sincos_rom[addr]                   BF16 codes, tools/gen_rope_rom.py
+//   x' = bf16(bf16(x*cos) - bf16(y*sin))            bf16_multiplier / bf16_subtractor
+//   y' = bf16(bf16(x*sin) + bf16(y*cos))            bf16_multiplier / bf16_adder
+// Each BF16 unit is the exact operation rounded to BF16 through FP32, the
+// reference's definition of the units (gen_bf16_primitive_vectors.py:31-32).
+// In FP32: the product of two BF16 values is exact, and an FP32 sum or
+// difference is the float32 rounding of the exact one, which is what
+// f32_to_bf16 rounds first; __float2bfloat16_rn is its second step.
+// One warp per row; lane l owns pairs 2l and 2l+1.
+#include "gqa_b200.h"
+#include "gqa_device.cuh"
+
+namespace gqa {
+
+namespace {
+
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__global__ void __launch_bounds__(256) rope_rtl_kernel(const __nv_bfloat16* x, __nv_bfloat16* out,
+                                                       const int32_t* __restrict__ pos, int rows, int heads,
+                                                       int64_t pos_stride, int64_t head_stride,
+                                                       const uint32_t* __restrict__ phase_rom,
+                                                       const uint32_t* __restrict__ sincos_rom, int addr_bits) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int i_pos = row / heads, h = row % heads;
+    const uint32_t p = (uint32_t)pos[i_pos];
+    const int64_t off = (int64_t)i_pos * pos_stride + (int64_t)h * head_stride;
+    const int i = 2 * lane;
+    const float2 xv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + off + i));
+    const float2 yv = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(x + off + i + kPairs));
+    float re[2], im[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const uint32_t phase = phase_rom[i + j] * p;  // wraps mod 2^32
+        const uint32_t cs = sincos_rom[phase >> (32 - addr_bits)];
+        const float c = __uint_as_float(cs & 0xffff0000u), s = __uint_as_float(cs << 16);
+        const float xj = j ? xv.y : xv.x, yj = j ? yv.y : yv.x;
+        const float xc = bf16_round(xj * c), ys = bf16_round(yj * s);
+        const float xs = bf16_round(xj * s), yc = bf16_round(yj * c);
+        re[j] = xc - ys;
+        im[j] = xs + yc;
+    }
+    *reinterpret_cast<__nv_bfloat162*>(out + off + i) = __floats2bfloat162_rn(re[0], re[1]);
+    *reinterpret_cast<__nv_bfloat162*>(out + off + i + kPairs) = __floats2bfloat162_rn(im[0], im[1]);
+}
+
+}  // namespace
+
+}  // namespace gqa
+
+extern "C" int gqa_rope_rtl(const void* x, void* out, const int32_t* positions, int n_positions, int heads,
+                            int64_t pos_stride, int64_t head_stride, const uint32_t* phase_rom,
+                            const uint32_t* sincos_rom, int rom_addr_bits, void* stream) {
+    if (!x || !out || !positions || !phase_rom || !sincos_rom) return GQA_ERR_NULL_POINTER;
+    if (n_positions < 0 || heads < 1 || heads > 4096) return GQA_ERR_BATCH;
+    if (rom_addr_bits < 1 || rom_addr_bits > 24) return GQA_ERR_GEOMETRY;
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(out) & 15u) || pos_stride % 8 ||
+        head_stride % 8)
+        return GQA_ERR_ALIGNMENT;
+    const int64_t rows = (int64_t)n_positions * heads;
+    if (rows == 0) return GQA_OK;
+    if (rows > 0x7fffffffLL) return GQA_ERR_BATCH;
+    gqa::rope_rtl_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), positions, (int)rows, heads,
+        pos_stride, head_stride, phase_rom, sincos_rom, rom_addr_bits);
+    return cudaGetLastError() == cudaSuccess ? GQA_OK : GQA_ERR_CUDA;
+}

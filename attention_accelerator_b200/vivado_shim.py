@@ -21,7 +21,10 @@ contract with the B200 library in place of the XSim testbench:
 * with INVALID_CONFIG, programs N_Q_HEADS=31 (tb :323) and passes only if the
   library rejects the start (tb :330-336).
 OUTPUT_BACKPRESSURE only throttles the RTL's AXIS egress; it has no GPU meaning
-and is accepted and ignored.
+and is accepted and ignored.  With GQA_RTL_NUMERICS=1 the decode reproduces the
+RTL's RoPE (ROM NCO, BF16 units) and BF16 scale register (``rtl_numerics``), so
+``gqa_rtl_out.mem`` approximates what the RTL testbench would write; the check
+against the golden then reports those quantisations as the RTL would show them.
 """
 from __future__ import annotations
 
@@ -90,7 +93,8 @@ def main(argv: list[str] | None = None) -> int:
     v = load("gqa_v.mem", 16).view(torch.bfloat16).reshape(8, -1, 128)
     golden = load("gqa_golden.mem", 128).cpu().numpy().view(np.uint16)
     try:
-        out = decode(q, k, v, seq_len=seq_len, query_position=qpos, kv_block_len=kv_block_len, layout="head_major")
+        out = decode(q, k, v, seq_len=seq_len, query_position=qpos, kv_block_len=kv_block_len, layout="head_major",
+                     rtl_numerics=os.environ.get("GQA_RTL_NUMERICS", "0") not in ("", "0"))
     except GqaConfigError as exc:
         print(f"FAIL: configuration rejected: {exc}")
         return 1

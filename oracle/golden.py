@@ -100,7 +100,8 @@ class _Neumaier:
 def gqa_golden_f64(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray,
                    seq_len: int, query_position: int, *, group: int = 4,
                    theta: float = ROPE_THETA, exact: bool = True,
-                   pos_chunk: int = 2048, k_rotated: bool = False) -> np.ndarray:
+                   pos_chunk: int = 2048, k_rotated: bool = False, q_rotated: bool = False,
+                   scale: float | None = None) -> np.ndarray:
     """Float64 attention output ``[n_q_heads, D]`` before the final BF16 rounding.
 
     ``q_bits``: ``[n_q, D]`` BF16 codes; ``k_bits``/``v_bits``: ``[n_kv, >=seq_len, D]``
@@ -108,15 +109,18 @@ def gqa_golden_f64(q_bits: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray,
     Keys ``p`` in ``[0, query_position]`` contribute (:132-133); rows past that are
     never read, which is the pad/causal mask of :83 and :125-126.
     ``k_rotated``: ``k_bits`` already hold rotated keys (a pre-rotated K cache), so
-    the per-key rope_half_split of :122-124 is skipped; Q is rotated as always.
+    the per-key rope_half_split of :122-124 is skipped; ``q_rotated`` likewise for
+    Q.  ``scale`` replaces the exact 1/sqrt(D) of :129 (the RTL-numerics mode uses
+    the BF16 SCALE_FACTOR register value).
     """
     if not 0 <= query_position < seq_len:
         raise ValueError("query_position must be in [0, seq_len)")
     n_q, d = q_bits.shape
     n_vis = query_position + 1
     head_of = np.arange(n_q) // group                           # gqa_controller.v:159-162
-    scale = 1.0 / math.sqrt(d)
-    q_ref = rope_half_split(bf16_to_f32(q_bits)[None], [query_position], theta, exact)[0]
+    scale = 1.0 / math.sqrt(d) if scale is None else float(scale)
+    q_ref = (bf16_to_f32(q_bits) if q_rotated
+             else rope_half_split(bf16_to_f32(q_bits)[None], [query_position], theta, exact)[0])
 
     # Scores, one slab of key positions at a time (bounded memory at 131072 keys).
     scores = np.empty((n_q, n_vis), dtype=np.float64)

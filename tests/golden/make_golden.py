@@ -7,6 +7,8 @@ reference's generators:
     ``run_gqa_regression.py:13-20`` cases, the README 65,536-element corpus, the
     default smoke corpus, and extra causal / block-length / longer cases);
   * ``pyfiles/gen_rope_test_vectors.py`` (512-row RoPE known-answer set);
+  * ``pyfiles/gen_bf16_primitive_vectors.py`` (65,536 BF16 add/multiply
+    conformance cases, the reference's definition of its BF16 units);
   * ``tools/gen_rope_rom.py`` at 10 and 14 address bits, and ``pyfiles/gen_rope_rom.py``.
 It records the sha256 of every file they write in ``manifest.json`` and copies
 each case's ``gqa_golden.mem`` and ``gqa_config.txt`` under ``cases/<name>/``.
@@ -67,7 +69,8 @@ def main() -> None:
     args = ap.parse_args()
     ref = args.reference.resolve()
     py = [sys.executable, "-B"]
-    manifest = {"python": sys.version.split()[0], "cases": {}, "rope_kat": {}, "rope_rom": {}}
+    manifest = {"python": sys.version.split()[0], "cases": {}, "rope_kat": {}, "rope_rom": {},
+                "bf16_primitives": {}}
     with tempfile.TemporaryDirectory() as tmp:
         tmp = Path(tmp)
         for name, extra in CASES:
@@ -84,6 +87,10 @@ def main() -> None:
         run(py + [str(ref / "pyfiles/gen_rope_test_vectors.py"), "--out-dir", str(out)])
         manifest["rope_kat"] = {"rows": 512, "seed": 20260805,
                                 "sha256": {f: sha256(out / f) for f in ("in.mem", "golden.mem")}}
+        out = tmp / "bf16"
+        run(py + [str(ref / "pyfiles/gen_bf16_primitive_vectors.py"), "--out-dir", str(out)])
+        manifest["bf16_primitives"] = {"cases": 65536, "seed": 20260805, "sha256": {
+            f: sha256(out / f) for f in ("a.mem", "b.mem", "add_golden.mem", "mul_golden.mem")}}
         for bits in (10, 14):
             out = tmp / f"rom{bits}"
             run(py + [str(ref / "tools/gen_rope_rom.py"), "--out-dir", str(out), "--rom-addr-bits", str(bits)])

@@ -26,33 +26,12 @@ import torch
 import attention_accelerator_b200 as gqa
 from attention_accelerator_b200 import _lib
 from attention_accelerator_b200.api import make_params
-from conftest import bits_to_torch, torch_to_bits
+from conftest import assert_chunk_parity, bits_to_torch, torch_to_bits
 from oracle import check_rows, chunked_golden_f64
 from oracle.bf16 import bf16_to_f32, f32_to_bf16, ulp_distance
 
 pytestmark = pytest.mark.gpu
 
-CANCEL_FLOOR = 2.0 ** -18   # below this fraction of the row max the 64-ULP rule is not FP32-attainable
-ABS_BOUND = 2.0 ** -20      # absolute bound there, as a fraction of the row max
-
-
-def assert_chunk_parity(golden64, got, tight: int = 2):
-    """The bound of the module docstring; returns the count of strict-rule exceptions."""
-    golden = f32_to_bf16(np.asarray(golden64)).reshape(-1, 128)
-    g64 = np.asarray(golden64, dtype=np.float64).reshape(-1, 128)
-    got = np.asarray(got).reshape(-1, 128)
-    res = check_rows(golden, got, 64)
-    dist = ulp_distance(golden, got)
-    rowmax = np.abs(g64).max(axis=-1, keepdims=True)
-    strict = np.abs(g64) >= CANCEL_FLOOR * rowmax
-    exempt = ((golden.astype(np.int64) >> 7) & 0xFF) <= 0x3D
-    assert not np.any((dist > 64) & strict & ~exempt), res.line()
-    err = np.abs(bf16_to_f32(got).astype(np.float64) - g64)
-    assert np.all(strict | (err <= ABS_BOUND * rowmax)), float((err / rowmax)[~strict].max())
-    big = np.abs(g64) >= np.ldexp(rowmax, -10)
-    assert int(dist[big].max(initial=0)) <= tight, res.line()
-    assert res.mean_ulp < 0.1, res.line()
-    return int(np.sum((dist > 64) & ~exempt))
 
 
 def chunk_inputs(batch: int, n: int, seq_len: int, seed: int):

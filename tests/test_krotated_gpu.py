@@ -28,8 +28,7 @@ import torch
 
 import attention_accelerator_b200 as gqa
 from attention_accelerator_b200 import _lib
-from conftest import assert_parity, bits_to_torch, torch_to_bits
-from oracle import gqa_golden
+from conftest import assert_chunk_parity, bits_to_torch, torch_to_bits
 from oracle.bf16 import bf16_to_f32, f32_to_bf16, ulp_distance
 from oracle.golden import gqa_golden_f64, rope_half_split
 
@@ -95,7 +94,8 @@ def test_decode_rotated_cache(seq_len, layout, cuda_device):
     got = torch_to_bits(gqa.decode(bits_to_torch(q, cuda_device), kd, vd, layout=layout, k_rotated=True))
     chunk = 8192 if seq_len > 8192 else 2048
     # same keys: the decode kernel's usual bar against the float64 oracle
-    assert_parity(gqa_golden(q, k_rot, v, seq_len, seq_len - 1, exact=False, k_rotated=True, pos_chunk=chunk), got)
+    assert_chunk_parity(gqa_golden_f64(q, k_rot, v, seq_len, seq_len - 1, exact=False, k_rotated=True,
+                                       pos_chunk=chunk), got)
     # against the reference golden from the unrotated keys: within the effect of
     # rounding the rotated keys to BF16
     ref = gqa_golden_f64(q, k, v, seq_len, seq_len - 1, exact=False, pos_chunk=chunk)
@@ -116,7 +116,8 @@ def test_batched_ragged_rotated(cuda_device):
                                          k_rotated=True))
     for i, n in enumerate(lens):
         k_rot = k_all[:, starts[i]:starts[i] + n]
-        assert_parity(gqa_golden(seqs[i][0], k_rot, seqs[i][2], n, n - 1, exact=False, k_rotated=True), out[i])
+        assert_chunk_parity(gqa_golden_f64(seqs[i][0], k_rot, seqs[i][2], n, n - 1, exact=False, k_rotated=True),
+                            out[i])
 
 
 def test_flags_validation(cuda_device):

@@ -123,3 +123,47 @@ def test_generator_argument_checks():
         generate_case(target_input_vectors=65537)
     with pytest.raises(ValueError):
         generate_case(10, kv_block_len=0)
+
+
+def _primitive_vectors(cases: int = 65536, seed: int = 20260805):
+    """The operands of pyfiles/gen_bf16_primitive_vectors.py:26-30 (all a, then all b)."""
+    import random
+    rng = random.Random(seed)
+    a = f32_to_bf16(np.array([rng.uniform(-0.25, 0.25) for _ in range(cases)]))
+    b = f32_to_bf16(np.array([rng.uniform(-0.25, 0.25) for _ in range(cases)]))
+    return a, b
+
+
+def test_bf16_unit_semantics_match_reference_conformance_vectors(manifest):
+    """The RTL's BF16 adder and multiplier as the reference defines them for
+    conformance (gen_bf16_primitive_vectors.py:31-32): float64 result of the two
+    BF16 operands, rounded by f32_to_bf16.  The oracle's RTL-numerics RoPE uses
+    exactly these operations; here they reproduce the reference's own files."""
+    a, b = _primitive_vectors()
+    fa, fb = bf16_to_f32(a), bf16_to_f32(b)
+
+    def words(x):
+        return ("\n".join(f"{int(w):04x}" for w in x) + "\n").encode()
+    want = manifest["bf16_primitives"]["sha256"]
+    assert hashlib.sha256(words(a)).hexdigest() == want["a.mem"]
+    assert hashlib.sha256(words(b)).hexdigest() == want["b.mem"]
+    assert hashlib.sha256(words(f32_to_bf16(fa + fb))).hexdigest() == want["add_golden.mem"]
+    assert hashlib.sha256(words(f32_to_bf16(fa * fb))).hexdigest() == want["mul_golden.mem"]
+
+
+def test_rtl_rope_restatement():
+    """oracle.rtl follows rope_unit.v: 32-bit NCO phase, top 14 bits into the BF16
+    sincos ROM, rotation through BF16 multiply/subtract/add.  No RTL output dump
+    exists to pin it end to end; its parts are pinned (ROMs above, BF16 units
+    above), and against the float64 RoPE known-answer rows it stays within the
+    BF16 units' error: 2^-7 of the row pair's magnitude."""
+    from oracle.rtl import rom_factors, rope_rtl_rows
+    inp, gold = rope_kat()
+    got = rope_rtl_rows(inp, np.arange(512))
+    x = bf16_to_f32(inp)
+    mag = np.abs(x[:, :64]) + np.abs(x[:, 64:])
+    err = np.abs(bf16_to_f32(got) - bf16_to_f32(gold))
+    assert (err <= 2.0 ** -7 * np.concatenate([mag, mag], axis=1) + 2.0 ** -8 * np.abs(bf16_to_f32(gold))).all()
+    # the NCO: position 0 is angle 0 (cos 1, sin 0) for every pair
+    c, s = rom_factors([0])
+    assert (c == 0x3F80).all() and (s == 0).all()

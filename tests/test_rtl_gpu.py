@@ -1,0 +1,83 @@
+"""GPU tests of the RTL-numerics mode (gqa_rope_rtl, GQA_FLAG_Q_ROTATED).
+
+The reference RTL rotates Q and K with a ROM-based NCO and BF16 arithmetic
+units (rope_unit.v) and scales by the BF16 SCALE_FACTOR register (0x3DB5).
+``decode(..., rtl_numerics=True)`` reproduces those two quantisations and keeps
+the rest in FP32, so its output can be compared with a dump of the RTL
+datapath.  Checked here:
+  * gqa_rope_rtl bit for bit against the oracle's restatement of rope_unit.v
+    (oracle/rtl.py), for K rows (8 heads) and Q rows (32 heads), at positions
+    past the RTL's 16-bit position register too;
+  * RTL-numerics decode against the float64 oracle fed the same RTL-rotated Q
+    and K and the BF16 scale, at the decode kernel's usual bar;
+  * how far the modelled RTL sits from the reference golden: within 2^-5 of
+    each output row's RMS (measured up to 2.4 %; some near-zero outputs are
+    then beyond 64 ULP, which is where a real RTL dump would be expected to
+    miss the golden too).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import attention_accelerator_b200 as gqa
+from conftest import assert_chunk_parity, bits_to_torch, torch_to_bits
+from oracle.bf16 import bf16_to_f32
+from oracle.golden import gqa_golden_f64
+from oracle.rtl import rope_rtl_rows
+from oracle.vectors import rope_kat
+
+pytestmark = pytest.mark.gpu
+
+RTL_SCALE = 0.08837890625  # BF16 0x3DB5
+
+
+def _inputs(seq_len: int, seed: int):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn(s, generator=g) for s in ((32, 128), (8, seq_len, 128), (8, seq_len, 128)))
+    return tuple(torch_to_bits(t.to(torch.bfloat16)) for t in (q, k, v))
+
+
+def test_rope_rtl_bit_exact_on_the_known_answer_rows(cuda_device):
+    inp, _ = rope_kat()  # 512 rows at positions 0..511, one head each
+    x = bits_to_torch(inp.reshape(512, 1, 128), cuda_device)
+    got = torch_to_bits(gqa.rope_rtl(x, torch.arange(512, dtype=torch.int32))).reshape(512, 128)
+    np.testing.assert_array_equal(got, rope_rtl_rows(inp, np.arange(512)))
+
+
+@pytest.mark.parametrize("layout", ["position_major", "head_major"])
+def test_rope_rtl_bit_exact_k_and_q(layout, cuda_device):
+    q, k, _ = _inputs(3000, 21)
+    pos = np.concatenate([np.arange(1000), np.random.default_rng(4).integers(0, 1 << 20, 2000)])
+    kd = bits_to_torch(k if layout == "head_major" else k.transpose(1, 0, 2).copy(), cuda_device)
+    got = torch_to_bits(gqa.rope_rtl(kd, torch.as_tensor(pos, dtype=torch.int32), layout=layout))
+    got_hm = got if layout == "head_major" else got.transpose(1, 0, 2)
+    for h in range(8):
+        np.testing.assert_array_equal(got_hm[h], rope_rtl_rows(k[h], pos))
+    qd = bits_to_torch(q.reshape(1, 32, 128), cuda_device)
+    gq = torch_to_bits(gqa.rope_rtl(qd, torch.tensor([2999], dtype=torch.int32))).reshape(32, 128)
+    np.testing.assert_array_equal(gq, rope_rtl_rows(q, [2999] * 32))
+
+
+@pytest.mark.parametrize("seq_len", [30, 600, 4096, 5000])
+def test_decode_rtl_numerics(seq_len, cuda_device):
+    q, k, v = _inputs(seq_len, 500 + seq_len)
+    got = torch_to_bits(gqa.decode(bits_to_torch(q, cuda_device), bits_to_torch(k, cuda_device),
+                                   bits_to_torch(v, cuda_device), layout="head_major", rtl_numerics=True))
+    q_r = rope_rtl_rows(q, [seq_len - 1] * 32)
+    k_r = np.stack([rope_rtl_rows(k[h], np.arange(seq_len)) for h in range(8)])
+    # cancellation-aware bar: these inputs (BF16-rotated Q and K) leave more outputs
+    # as residues of cancelling terms than the plain path's tests meet
+    assert_chunk_parity(gqa_golden_f64(q_r, k_r, v, seq_len, seq_len - 1, exact=False, q_rotated=True,
+                                       k_rotated=True, scale=RTL_SCALE), got)
+    ref = gqa_golden_f64(q, k, v, seq_len, seq_len - 1, exact=False)
+    rms = np.sqrt((ref ** 2).mean(axis=1, keepdims=True))
+    assert (np.abs(bf16_to_f32(got) - ref) <= 2.0 ** -5 * rms).all()
+
+
+def test_rtl_numerics_refuses_a_rotated_cache(cuda_device):
+    q, k, v = _inputs(16, 1)
+    with pytest.raises(ValueError):
+        gqa.decode(bits_to_torch(q, cuda_device), bits_to_torch(k, cuda_device), bits_to_torch(v, cuda_device),
+                   layout="head_major", rtl_numerics=True, k_rotated=True)
