@@ -293,10 +293,14 @@ __device__ __forceinline__ void exchange_and_finish(const DecodeArgs& a, int h, 
     }
     named_barrier_sync(1, kConsumerThreads);
     if (tid == 0) {
+        // One system-scope release for all peers: the fence orders every push
+        // (ours, and the CTA's through the barrier above) before the flag
+        // stores, which then go out back to back instead of one NVLink round
+        // trip per peer.
         asm volatile("fence.acq_rel.sys;" ::: "memory");
         for (int p = 0; p < a.world; ++p) {
             uint32_t* flags = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(a.peer_bases[p]) + push);
-            st_release_sys(flags + a.rank * kNumKVHeads + h, e);
+            st_relaxed_sys(flags + a.rank * kNumKVHeads + h, e);
         }
     }
     // Thread r waits for source rank r's flag of head h in this rank's own buffer.
