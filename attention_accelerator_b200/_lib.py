@@ -112,6 +112,7 @@ _SIGNATURES = {
     "gqa_rope_k_cache": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, _P]),
     "gqa_rope_rtl": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, _P, _P,
                                     ctypes.c_int, _P]),
+    "gqa_chunked_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(GqaParams), ctypes.POINTER(GqaChunkParams)]),
     "gqa_mem_decode_workspace_bytes": (ctypes.c_size_t, [ctypes.c_size_t]),
     "gqa_mem_decode": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.c_int, _P, ctypes.c_uint64, _P, _P,
                                       ctypes.c_size_t, _P]),

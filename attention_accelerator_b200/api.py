@@ -206,7 +206,7 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, seq_len: int | 
 def decode_chunked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, first_position: int,
                    seq_len: int | None = None, kv_block_len: int = DEFAULT_KV_BLOCK_LEN,
                    scale: float | None = None, layout: str = "position_major", rope_theta: float = ROPE_THETA,
-                   out: torch.Tensor | None = None) -> torch.Tensor:
+                   out: torch.Tensor | None = None, split_last_wave: bool = True) -> torch.Tensor:
     """Chunked multi-query decode on the tensor cores.
 
     ``q``: BF16 ``[B, n, 32, 128]`` with n <= 128; query i of sequence b sits at
@@ -242,9 +242,14 @@ def decode_chunked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, first_p
                             q_query_stride=q.stride(1), out_query_stride=out.stride(1),
                             k_batch_stride=k.stride(0), v_batch_stride=v.stride(0))
     stream = _stream_ptr(device)
-    ws = _workspace(device, stream, _lib.CHUNKED_WORKSPACE_BYTES)
+    # With room for the partial rows the last, partly filled wave of (sequence,
+    # Q head) units is split along the keys (split_last_wave=False: every unit whole).
+    nbytes = _lib.CHUNKED_WORKSPACE_BYTES
+    if split_last_wave:
+        nbytes = max(nbytes, lib.gqa_chunked_workspace_bytes(ctypes.byref(p), ctypes.byref(c)))
+    ws = _workspace(device, stream, nbytes)
     _check(lib.gqa_decode_chunked(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), ctypes.byref(p),
-                                  ctypes.byref(c), ws.data_ptr(), ws.numel(), stream), "decode_chunked")
+                                  ctypes.byref(c), ws.data_ptr(), nbytes, stream), "decode_chunked")
     return out
 
 

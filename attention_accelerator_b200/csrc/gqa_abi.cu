@@ -603,11 +603,31 @@ int gqa_decode_chunked(const void* q, const void* k, const void* v, void* out, c
     l.n_queries = (int)c->n_queries;
     l.qscale = (float)((double)p->scale * 1.4426950408889634);
     l.status = static_cast<uint32_t*>(workspace);
+    // Split the last wave's units along the keys when the workspace holds their partials.
+    gqa::chunked_split_plan((int)c->batch, (int)p->seq_len, (int)c->first_position, (int)c->n_queries, sms,
+                            &l.full_units, &l.split);
+    const size_t part_bytes = gqa::chunked_partial_bytes((int)c->batch, l.full_units, l.split);
+    if (part_bytes == 0 || workspace_bytes < GQA_CHUNKED_WORKSPACE_BYTES + part_bytes) {
+        l.full_units = (int)c->batch * gqa::kNumQHeads;
+        l.split = 1;
+    } else {
+        l.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + GQA_CHUNKED_WORKSPACE_BYTES);
+    }
     bool out_of_slots = false;
     if (gqa::rope_table_for((double)p->rope_theta, &l.rope, &out_of_slots) != cudaSuccess) return GQA_ERR_CUDA;
     if (out_of_slots) return GQA_ERR_ROPE_THETA;
     if (gqa::launch_chunked(l, static_cast<cudaStream_t>(stream)) != cudaSuccess) return GQA_ERR_CUDA;
     return GQA_OK;
+}
+
+size_t gqa_chunked_workspace_bytes(const gqa_params* p, const gqa_chunk_params* c) {
+    if (!p || !c || c->batch < 1 || c->batch > 65535u || c->n_queries < 1) return 0;
+    int sms = 0;
+    if (current_device(&sms) != GQA_OK) return 0;
+    int full = 0, split = 1;
+    gqa::chunked_split_plan((int)c->batch, (int)p->seq_len, (int)c->first_position, (int)c->n_queries, sms, &full,
+                            &split);
+    return GQA_CHUNKED_WORKSPACE_BYTES + gqa::chunked_partial_bytes((int)c->batch, full, split);
 }
 
 int gqa_rope_rows(const void* x, const int32_t* positions, float* out, int rows, float rope_theta, void* stream) {

@@ -126,10 +126,17 @@ struct alignas(64) ChunkArgs {
     int seq_len;
     int first_pos;
     int n_queries;
-    int n_tiles;
+    int n_tiles;       // tiles of a whole (sequence, Q head) unit
     float qscale;
     uint32_t* status;
     const RopeTable* rope;
+    // Work split (grid is 1-D): CTAs [0, full_units) each take a whole unit
+    // (unit = b * 32 + qh) and write BF16 rows; every later unit is cut into
+    // `split` parts of consecutive tiles whose FP32 partial rows go to
+    // `partials` ([split unit][part][kRows][132]) for chunk_combine_kernel.
+    int full_units;
+    int split;
+    float* partials;
 };
 
 // ---- PTX wrappers -----------------------------------------------------------
@@ -286,9 +293,17 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int qh = blockIdx.x;     // Q head
-    const int kvh = qh / kGroup;   // its KV head
-    const int b = blockIdx.y;      // sequence
+    // Which unit (sequence, Q head) and which of its key tiles this CTA takes.
+    const int cta = blockIdx.x;
+    const bool partial = cta >= a.full_units;
+    const int part = partial ? (cta - a.full_units) % a.split : 0;
+    const int unit = partial ? a.full_units + (cta - a.full_units) / a.split : cta;
+    const int nparts = partial ? a.split : 1;
+    const int j0 = (int)((int64_t)a.n_tiles * part / nparts);
+    const int j1 = (int)((int64_t)a.n_tiles * (part + 1) / nparts);
+    const int qh = unit % kNumQHeads;  // Q head
+    const int kvh = qh / kGroup;       // its KV head
+    const int b = unit / kNumQHeads;   // sequence
     const RopeTable* rt = a.rope;
 
     if (threadIdx.x == 0) {
@@ -321,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_base_slot;
-    const int n_tiles = a.n_tiles;
+    const int n_tiles = j1 - j0;  // this CTA's tiles: absolute tiles j0 .. j1-1
 
     if (warp < kSoftmaxWarps) {
         // ======================= softmax: thread r owns query row r =======================
@@ -380,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
                 break;
             }
             tc_fence_after();
-            const int k0 = j * kTile;
+            const int k0 = (j0 + j) * kTile;
             // S = (block 2 + block 1) + block 0, in two load batches (one wait each).
             float s[kTile];
             float mx = -INFINITY;
@@ -422,6 +437,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
             const float m_new = fmaxf(m_run, mx);
             const float alpha = m_new == -INFINITY ? 1.f : exp2f(m_run - m_new);  // 0 for the first visible key
             m_run = m_new;
+            // A row with no visible key yet (possible in a later part of a split
+            // unit) exponentiates against 0: its P stays 0 rather than NaN.
+            const float m_use = m_run == -INFINITY ? 0.f : m_run;
             l *= alpha;
             // P(j) = 2^(s - m_run) split into three parts, in registers while O_tile(j-1) may still
             // be in flight (keys 2c, 2c+1 in column c of each part: the A operand of O_tile).
@@ -431,8 +449,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
             for (int c = 0; c < kTile; c += 2) {
                 // ex2(-inf) = 0 for masked keys; rows without any visible key (past
                 // n_queries) produce values that are never written out.
-                const float p0 = fast_exp2(s[c] - m_run);
-                const float p1 = fast_exp2(s[c + 1] - m_run);
+                const float p0 = fast_exp2(s[c] - m_use);
+                const float p1 = fast_exp2(s[c + 1] - m_use);
                 psum0 += p0;
                 psum1 += p1;
                 split3_fast(p0, p1, pp[0][c >> 1], pp[1][c >> 1], pp[2][c >> 1]);
@@ -475,16 +493,33 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
         }
         if (ok && warp_wait(pv_done, (n_tiles - 1) & 1)) {
             tc_fence_after();
-            // O = O(n-2) * alpha + O_tile(n-1), then O / l rounded to BF16.
+            // O = O(n-2) * alpha + O_tile(n-1), then O / l rounded to BF16, or for a
+            // part of a split unit the FP32 partial row (acc, m, l).
             __nv_bfloat16* orow =
                 a.out + (int64_t)b * a.o_bstride + (int64_t)r * a.o_istride + (int64_t)qh * a.o_hstride;
+            float* prow = partial ? a.partials + ((size_t)(cta - a.full_units) * kRows + r) * kPartialFloats
+                                  : nullptr;
+            if (partial && row_ok) {
+                prow[kHeadDim] = m_run;
+                prow[kHeadDim + 1] = l;
+            }
 #pragma unroll 1
             for (int q4 = 0; q4 < 4; ++q4) {
                 uint32_t ot[32], o[32];
                 tmem_ld32(lane_base + kColOT + 32 * q4, ot);
                 if (n_tiles > 1) tmem_ld32(lane_base + kColO + 32 * q4, o);
                 tmem_wait_ld();
-                if (row_ok) {
+                if (row_ok && partial) {
+#pragma unroll
+                    for (int c = 0; c < 32; c += 4) {
+                        float v4[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            v4[e] = n_tiles > 1 ? fmaf(__uint_as_float(o[c + e]), alpha_prev, __uint_as_float(ot[c + e]))
+                                                : __uint_as_float(ot[c + e]);
+                        *reinterpret_cast<float4*>(prow + 32 * q4 + c) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+                    }
+                } else if (row_ok) {
 #pragma unroll
                     for (int c = 0; c < 32; c += 8) {
                         float v8[8];
@@ -534,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
             float2 f[8];
             if (j % kReanchorTiles == 0) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) base[i] = rope_factor(rt->step[8 * c + i], (int64_t)j * kTile + kq);
+                for (int i = 0; i < 8; ++i) base[i] = rope_factor(rt->step[8 * c + i], (int64_t)(j0 + j) * kTile + kq);
             } else {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -586,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
         if (lane == 0) {
             bool ok = true;
             for (int j = 0; j < n_tiles && ok; ++j) {
-                const int row = j * kTile;
+                const int row = (j0 + j) * kTile;
                 const int c1 = a.kv_rows_inner ? row : kvh;
                 const int c2 = a.kv_rows_inner ? kvh : row;
                 const int st = j % kStages;
@@ -680,7 +715,58 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
     }
 }
 
+// LSE merge of a split unit's parts (the reference's flash-softmax rescale,
+// flash_softmax.v:233-512, output_accumulator.v:398-687, across key ranges):
+// one CTA per (split unit, query row), one thread per dim.
+__global__ void __launch_bounds__(kHeadDim) chunk_combine_kernel(const float* __restrict__ partials, int full_units,
+                                                                 int split, int n_queries, __nv_bfloat16* out,
+                                                                 int64_t o_bstride, int64_t o_istride,
+                                                                 int64_t o_hstride) {
+    const int su = blockIdx.x / n_queries, r = blockIdx.x % n_queries;
+    const int unit = full_units + su;
+    const int b = unit / kNumQHeads, qh = unit % kNumQHeads;
+    const int d = threadIdx.x;
+    auto row = [&](int p) { return partials + ((size_t)(su * split + p) * kRows + r) * kPartialFloats; };
+    float M = -INFINITY;
+    for (int p = 0; p < split; ++p) M = fmaxf(M, row(p)[kHeadDim]);
+    const float Mu = M == -INFINITY ? 0.f : M;
+    float L = 0.f, O = 0.f;
+    for (int p = 0; p < split; ++p) {
+        const float* x = row(p);
+        const float f = exp2f(x[kHeadDim] - Mu);
+        L = fmaf(x[kHeadDim + 1], f, L);
+        O = fmaf(x[d], f, O);
+    }
+    out[(int64_t)b * o_bstride + (int64_t)r * o_istride + (int64_t)qh * o_hstride + d] = __float2bfloat16_rn(O / L);
+}
+
 }  // namespace
+
+void chunked_split_plan(int batch, int seq_len, int first_pos, int n_queries, int sms, int* full_units, int* split) {
+    // The units of the last, partly filled wave are cut along the keys so
+    // that they fill it: with U units on `sms` SMs the rem = U mod sms units
+    // left after the full waves become rem * s CTAs, s = floor(sms / rem),
+    // each part at least kMinPartTiles tiles.
+    constexpr int kMinPartTiles = 4;
+    const int units = batch * kNumQHeads;
+    const int n_keys = first_pos + n_queries < seq_len ? first_pos + n_queries : seq_len;
+    const int n_tiles = (n_keys + kTile - 1) / kTile;
+    const int rem = units % sms;
+    int s = rem ? sms / rem : 1;
+    if (s > n_tiles / kMinPartTiles) s = n_tiles / kMinPartTiles;
+    if (s < 2) {
+        *full_units = units;
+        *split = 1;
+    } else {
+        *full_units = units - rem;
+        *split = s;
+    }
+}
+
+size_t chunked_partial_bytes(int batch, int full_units, int split) {
+    if (split < 2) return 0;
+    return (size_t)(batch * kNumQHeads - full_units) * split * kRows * kPartialFloats * sizeof(float);
+}
 
 size_t chunked_smem_bytes() { return kSmemBytes; }
 int chunked_max_queries() { return kRows; }
@@ -712,7 +798,16 @@ cudaError_t launch_chunked(const ChunkLaunch& l, cudaStream_t stream) {
     a.qscale = l.qscale;
     a.status = l.status;
     a.rope = l.rope;
-    chunked_kernel<<<dim3(kNumQHeads, l.batch), kThreads, kSmemBytes, stream>>>(a);
+    const int units = l.batch * kNumQHeads;
+    a.full_units = l.split >= 2 ? l.full_units : units;
+    a.split = l.split >= 2 ? l.split : 1;
+    a.partials = l.partials;
+    const int split_units = units - a.full_units;
+    chunked_kernel<<<a.full_units + split_units * a.split, kThreads, kSmemBytes, stream>>>(a);
+    if (split_units > 0)
+        chunk_combine_kernel<<<split_units * l.n_queries, kHeadDim, 0, stream>>>(
+            l.partials, a.full_units, a.split, l.n_queries, static_cast<__nv_bfloat16*>(l.out), l.o_bstride,
+            l.o_istride, l.o_hstride);
     return cudaGetLastError();
 }
 

@@ -51,7 +51,11 @@ struct ChunkLaunch {
     float qscale;
     uint32_t* status;
     const RopeTable* rope;
+    int full_units, split;  // key-range split of the last wave's units (chunked_split_plan)
+    float* partials;        // chunked_partial_bytes of workspace for their partial rows
 };
+void chunked_split_plan(int batch, int seq_len, int first_pos, int n_queries, int sms, int* full_units, int* split);
+size_t chunked_partial_bytes(int batch, int full_units, int split);
 size_t chunked_smem_bytes();
 int chunked_max_queries();
 int chunked_tile_keys();

@@ -129,3 +129,36 @@ def test_chunked_config_errors_rejected(cuda_device):
     assert call(4, 0, scale=0.0) == _lib.GQA_ERR_SCALE
     torch.cuda.synchronize()
     assert not torch.any(out.view(torch.int16) != 0)
+
+
+def test_split_last_wave_mixed_with_whole_units(cuda_device):
+    """Batch 5 = 160 (sequence, Q head) units on 148 SMs: 148 run whole, the
+    other 12 are split along the keys and merged by the combine kernel.  Both
+    kinds against the oracle, and against the unsplit run."""
+    b, n, s = 5, 128, 2048
+    q, k, v = chunk_inputs(b, n, s, seed=55)
+    qd = bits_to_torch(q, cuda_device)
+    kd = bits_to_torch(k.transpose(0, 2, 1, 3), cuda_device)
+    vd = bits_to_torch(v.transpose(0, 2, 1, 3), cuda_device)
+    split = torch_to_bits(gqa.decode_chunked(qd, kd, vd, first_position=s - n, seq_len=s))
+    whole = torch_to_bits(gqa.decode_chunked(qd, kd, vd, first_position=s - n, seq_len=s, split_last_wave=False))
+    torch.cuda.synchronize()
+    assert gqa.read_device_status(cuda_device) == 0
+    golden = chunked_golden_f64(q, k, v, s, s - n)
+    assert_chunk_parity(golden, split)
+    assert_chunk_parity(golden, whole)
+
+
+def test_chunked_workspace_sizes(cuda_device):
+    """The split's workspace covers its partial rows; a 256-byte workspace runs every unit whole."""
+    lib = _lib.load()
+    p = make_params(seq_len=8192, query_position=8191)
+    c = _lib.GqaChunkParams(batch=16, n_queries=128, first_position=8064)
+    need = lib.gqa_chunked_workspace_bytes(ctypes.byref(p), ctypes.byref(c))
+    sms = torch.cuda.get_device_properties(cuda_device).multi_processor_count
+    rem = (16 * 32) % sms
+    if rem:
+        assert need >= _lib.CHUNKED_WORKSPACE_BYTES + rem * 2 * 128 * 132 * 4
+    c1 = _lib.GqaChunkParams(batch=1, n_queries=37, first_position=100)
+    p1 = make_params(seq_len=1000, query_position=136)
+    assert lib.gqa_chunked_workspace_bytes(ctypes.byref(p1), ctypes.byref(c1)) == _lib.CHUNKED_WORKSPACE_BYTES
