@@ -10,6 +10,8 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <queue>
+#include <vector>
 #include <mutex>
 
 static_assert(sizeof(gqa_seq_desc) == sizeof(gqa::SeqDesc), "descriptor layout");
@@ -24,6 +26,7 @@ constexpr int kMinChunk = gqa::kDecodeTileKeys;  // keys: one pipeline tile
 constexpr int kMinChunkMultiWave = 256;
 constexpr int kMaxWaves = 16;
 constexpr int kOverheadKeys = 64;    // per-CTA prologue/epilogue cost, in key-equivalents
+constexpr int kBatchOverheadKeys = 128;  // the same for a batch's splits (they also pass through split_merge_kernel)
 // What merging a single sequence's splits adds to its latency, in pipeline
 // tiles of one CTA: the last split's arrival and L2 round trip, or a cluster
 // barrier and distributed-shared-memory round trip.
@@ -228,6 +231,37 @@ Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = f
         return s;
     };
     auto round8 = [](int64_t x) { return (int)(((x + 7) / 8) * 8); };
+    // A batch runs its full-chunk splits first and the shorter last splits after
+    // them (decode_kernel's CTA order).  Its cost: that order scheduled greedily
+    // on sms/8 machines (the 8 CTAs of a split, one per KV head, side by side),
+    // in key-equivalents with a fixed per-split overhead.
+    std::vector<int64_t> rems;
+    auto schedule_cost = [&](int c) {
+        const int machines = std::max(1, slots);
+        int64_t full = 0;
+        rems.clear();
+        for (int b = 0; b < batch; ++b) {
+            const int64_t n = gqa::seq_key_count(d[b]);
+            full += n / c;
+            if (gqa::seq_splits(d[b], c) > n / c) rems.push_back(n % c);
+        }
+        const double job = (double)c + kBatchOverheadKeys;
+        std::priority_queue<double, std::vector<double>, std::greater<double>> free_at;
+        for (int m = 0; m < machines; ++m)
+            free_at.push((double)(full / machines + (m < full % machines ? 1 : 0)) * job);
+        double end = 0;
+        for (const int64_t r : rems) {
+            const double t = free_at.top() + (double)r + kBatchOverheadKeys;
+            free_at.pop();
+            free_at.push(t);
+            end = std::max(end, t);
+        }
+        while (!free_at.empty()) {
+            end = std::max(end, free_at.top());
+            free_at.pop();
+        }
+        return end;
+    };
     int best_chunk = 0;
     double best_cost = 0;
     const int max_w = batch == 1 ? 1 : kMaxWaves;
@@ -239,7 +273,7 @@ Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = f
         const int c = round8(chunk);
         const int64_t ctas = splits_for(c) * gqa::kNumKVHeads;
         const int64_t waves = (ctas + sms - 1) / sms;
-        const double cost = (double)waves * (double)(c + kOverheadKeys);
+        const double cost = batch == 1 ? (double)waves * (double)(c + kOverheadKeys) : schedule_cost(c);
         if (best_chunk == 0 || cost < best_cost) {
             best_chunk = c;
             best_cost = cost;

@@ -516,37 +516,67 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     allow_dependent_launch();
     grid_dependency_wait();
 
-    // ---- which (sequence, split) this CTA owns: prefix sum of splits per sequence,
-    // computed by the producer warp, which goes on to issue the loads at once;
-    // the consumers pick the result up through named barrier 2.
+    // ---- which (sequence, split) this CTA owns, computed by the producer warp,
+    // which goes on to issue the loads at once; the consumers pick the result up
+    // through named barrier 2.  A batch runs every sequence's full-chunk splits
+    // first and the shorter last splits after them, so that those fill the last
+    // wave; partials are stored by the logical index prefix_splits[b] + split,
+    // contiguous per sequence for the split merge.
     if (warp == kConsumerWarps) {
-        int b = 0, split = gsplit;
+        int b = 0, split = gsplit, logical = gsplit;
         if (!single) {
-            int base = 0;
-            b = -1;
-            for (int b0 = 0; b0 < a.batch && b < 0; b0 += 32) {
-                const int bb = b0 + lane;
-                const int ns = bb < a.batch ? seq_splits(a.descs[bb], a.chunk) : 0;
-                int incl = ns;
+            // Sequence b has full_b = keys / chunk full splits and
+            // seq_splits - full_b (0 or 1) shorter last ones.
+            auto counts = [&](int bb, int& nf, int& np) {
+                nf = np = 0;
+                if (bb < a.batch) {
+                    const SeqDesc db = a.descs[bb];
+                    nf = seq_key_count(db) / a.chunk;
+                    np = seq_splits(db, a.chunk) - nf;
+                }
+            };
+            auto scan = [&](int v) {
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
-                    const int t = __shfl_up_sync(0xffffffffu, incl, o);
-                    if (lane >= o) incl += t;
+                    const int t = __shfl_up_sync(0xffffffffu, v, o);
+                    if (lane >= o) v += t;
                 }
-                const int excl = incl - ns;
-                const bool hit = bb < a.batch && gsplit >= base + excl && gsplit < base + incl;
+                return v;
+            };
+            int total_full = 0;
+            for (int b0 = 0; b0 < a.batch; b0 += 32) {
+                int nf, np;
+                counts(b0 + lane, nf, np);
+                total_full += __shfl_sync(0xffffffffu, scan(nf), 31);
+            }
+            const bool in_full = gsplit < total_full;
+            const int target = in_full ? gsplit : gsplit - total_full;
+            int base = 0, sbase = 0;  // splits of the chosen kind / of any kind before b0
+            b = -1;
+            for (int b0 = 0; b0 < a.batch && b < 0; b0 += 32) {
+                int nf, np;
+                counts(b0 + lane, nf, np);
+                const int nk = in_full ? nf : np;
+                const int incl = scan(nk), sincl = scan(nf + np);
+                const int excl = incl - nk;
+                const bool hit = b0 + lane < a.batch && target >= base + excl && target < base + incl;
                 const unsigned m = __ballot_sync(0xffffffffu, hit);
                 if (m) {
                     const int src = __ffs(m) - 1;
                     b = b0 + src;
-                    split = gsplit - base - __shfl_sync(0xffffffffu, excl, src);
+                    const int nf_src = __shfl_sync(0xffffffffu, nf, src);
+                    split = in_full ? target - base - __shfl_sync(0xffffffffu, excl, src) : nf_src;
+                    const int sexcl = __shfl_sync(0xffffffffu, sincl - (nf + np), src);
+                    logical = sbase + sexcl + split;
                 }
                 base += __shfl_sync(0xffffffffu, incl, 31);
+                sbase += __shfl_sync(0xffffffffu, sincl, 31);
             }
         }
         if (lane == 0) {
             info[0] = b;
             info[1] = split;
+            info[5] = logical;
         }
         __syncwarp();
         named_barrier_arrive(2, kThreads);
@@ -555,6 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
     const int b = info[0];
     const int split = info[1];
+    const int lsplit = info[5];  // storage index of this split's partial
     if (b < 0) return;  // grid larger than the plan: nothing to do (uniform per CTA)
     const SeqDesc d = single ? a.single : a.descs[b];
     const int n_keys = seq_key_count(d);
@@ -566,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const int64_t first_row = d.kv_start + key0;
 
     // The split merge finds each sequence's splits here.
-    if (!clustered && split == 0 && h == 0 && tid == 0 && n_split > 1) a.ws_seqinfo[b] = make_int2(gsplit, n_split);
+    if (!clustered && split == 0 && h == 0 && tid == 0 && n_split > 1) a.ws_seqinfo[b] = make_int2(lsplit, n_split);
 
     // ======================= producer warp =======================
     // In a cluster the whole warp also takes part in the epilogue's two cluster
@@ -831,7 +862,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     // Thread t < 128 merges head t / 32, dims 4 (t % 32) .. +3.
     float* part = clustered                     ? cpart
                   : (exchange && n_split == 1) ? xrows
-                                               : a.ws_partials + ((int64_t)gsplit * kNumKVHeads + h) * kGroup * kPartialFloats;
+                                               : a.ws_partials + ((int64_t)lsplit * kNumKVHeads + h) * kGroup * kPartialFloats;
     if (tid < kOutputs / 4) {
         const int hq = tid >> 5, d0 = (tid & 31) * 4;
         float4 O = make_float4(0.f, 0.f, 0.f, 0.f);

@@ -173,3 +173,16 @@ def test_fixed_width_shape_and_look_alikes(variant, cuda_device, tmp_path):
             memfile.decode_mem(data, 16)
         return
     np.testing.assert_array_equal(_gpu(data, 16), want)
+
+
+def test_general_parser_at_scale(cuda_device):
+    """A 41 MB CRLF file (the fixed-width fast path does not apply) is larger than
+    the general parser's grid of 148 x 8 blocks x 16 KB, so every block walks
+    several chunks; the decode equals the rows it was written from."""
+    g = torch.Generator().manual_seed(9)
+    rows = torch.randint(-32768, 32767, (600_000, 16), generator=g, dtype=torch.int16)
+    host = rows.numpy().view(np.uint16)
+    text = host_encode(host).replace(b"\n", b"\r\n")
+    assert len(text) > 148 * 8 * 16384
+    back = memfile.decode_mem(text, 16)
+    assert torch.equal(back.cpu(), rows)
