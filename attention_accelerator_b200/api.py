@@ -421,12 +421,14 @@ _rtl_roms: dict = {}
 
 
 def _rtl_rom_tables(device: torch.device, rope_theta: float, bits: int):
+    """Device copies of the phase and sincos ROMs, built once per (device, theta, bits)."""
     key = (device, float(rope_theta), bits)
-    if key not in _rtl_roms:
-        phase = torch.tensor(rope_phase_rom(HEAD_DIM, rope_theta), dtype=torch.int64).to(torch.int32)
-        sincos = torch.tensor(rope_sincos_rom(bits), dtype=torch.int64).to(torch.int32)
-        _rtl_roms[key] = (phase.to(device), sincos.to(device))
-    return _rtl_roms[key]
+    with _ws_lock:
+        if key not in _rtl_roms:
+            phase = torch.tensor(rope_phase_rom(HEAD_DIM, rope_theta), dtype=torch.int64).to(torch.int32)
+            sincos = torch.tensor(rope_sincos_rom(bits), dtype=torch.int64).to(torch.int32)
+            _rtl_roms[key] = (phase.to(device), sincos.to(device))
+        return _rtl_roms[key]
 
 
 def rope_rtl(x: torch.Tensor, positions: torch.Tensor, *, layout: str = "position_major",
