@@ -251,12 +251,15 @@ constexpr int kMergeBatch = 20;  // splits whose acc values a thread loads befor
 static_assert(2 * kConsumerThreads >= kOutputs, "two outputs per consumer thread cover the head group");
 static_assert(kConsumerWarps >= kGroup, "one warp per Q head reduces (m, l)");
 
-__device__ __forceinline__ uint32_t arrive_relaxed_gpu(uint32_t* p) {
+// Arrival of one split: releases the CTA's partial stores (ordered before it
+// through the CTA barrier; release is cumulative) and, for the last split,
+// acquires every earlier split's -- one acq_rel atomic instead of a fence on
+// either side of a relaxed one.
+__device__ __forceinline__ uint32_t arrive_acq_rel_gpu(uint32_t* p) {
     uint32_t old;
-    asm volatile("atom.relaxed.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(p) : "memory");
     return old;
 }
-__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 constexpr int kLastMergeScratchFloats = kGroup * kLastMergeMaxSplits + 2 * kGroup;
 
@@ -366,13 +369,9 @@ __device__ __forceinline__ void last_split_merge(const DecodeArgs& a, int n, int
                                                  const OutSpec& direct, float* xrows, int* info) {
     named_barrier_sync(1, kConsumerThreads);  // every partial store of this CTA is issued
     if (tid == 0) {
-        fence_acq_rel_gpu();  // ... and ordered before the arrival (cumulative through the barrier)
-        const uint32_t prev = arrive_relaxed_gpu(a.ws_arrivals + h);
+        const uint32_t prev = arrive_acq_rel_gpu(a.ws_arrivals + h);
         const int last = prev == (uint32_t)(n - 1);
-        if (last) {
-            a.ws_arrivals[h] = 0u;  // the next call's kernel starts after this one completes
-            fence_acq_rel_gpu();    // the other splits' partials are visible to the loads below
-        }
+        if (last) a.ws_arrivals[h] = 0u;  // the next call's kernel starts after this one completes
         *flag = last;
     }
     named_barrier_sync(1, kConsumerThreads);
