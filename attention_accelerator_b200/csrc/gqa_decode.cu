@@ -657,6 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     auto qk_tile = [&](int t, float (&sc)[kSteps]) {
         const uint8_t* kt = smem + (t % kStages) * kStageBytes;
         const int rows = min(kTileKeys, cnt - t * kTileKeys);
+        float2 ur[4], ui[4];  // this lane's factors at step `step`: w * (e^{i theta 4})^step
 #pragma unroll
         for (int step = 0; step < kSteps; ++step) {
             const int r = c * kKeysPerWarp + step * 4 + slot;
@@ -672,7 +673,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                     ri[jj] = bf16x2_to_float2(yw[jj]);
                 }
             } else {
-            float2 ur[4], ui[4];
             if (step == 0) {
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
@@ -681,7 +681,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 }
             } else {
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) cmul2(wr[jj], wi[jj], sr[jj], si[jj], ur[jj], ui[jj]);
+                for (int jj = 0; jj < 4; ++jj) {
+                    float2 nr, ni;
+                    cmul2(ur[jj], ui[jj], sr[jj], si[jj], nr, ni);
+                    ur[jj] = nr;
+                    ui[jj] = ni;
+                }
             }
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj)
