@@ -512,6 +512,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     };
     if (single && warp < kConsumerWarps)
         lane_rope(a.single.query_position, (int64_t)a.single.pos_begin + (int64_t)gsplit * a.chunk);
+    // A single sequence's split needs no memory read to know its keys: pull its
+    // Q rows and first K/V tiles into L2 while the previous kernel in the stream
+    // finishes (its loads below then hit L2).
+    if (single && tid == kConsumerThreads) {
+        const int n_keys = seq_key_count(a.single);
+        const int key0 = gsplit * a.chunk;
+        const int cnt = max(0, min(a.chunk, n_keys - key0));
+        const int n_pre = min((cnt + kTileKeys - 1) / kTileKeys, kStages);
+        for (int hq = 0; hq < kGroup; ++hq) bulk_prefetch_l2(a.q + (int64_t)(h * kGroup + hq) * a.q_hstride, kRowBytes);
+        for (int t = 0; t < n_pre; ++t) {
+            const int row = static_cast<int>(a.single.kv_start + key0 + (int64_t)t * kTileKeys);
+            tma_prefetch_3d(&a.kmap, 0, a.kv_rows_inner ? row : h, a.kv_rows_inner ? h : row);
+            tma_prefetch_3d(&a.vmap, 0, a.kv_rows_inner ? row : h, a.kv_rows_inner ? h : row);
+        }
+    }
     allow_dependent_launch();
     grid_dependency_wait();
 
