@@ -71,8 +71,9 @@ constexpr int kVStageBytes = 2 * kVBlockBytes;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kRotWarps = 4;
 constexpr int kProducerWarp = kSoftmaxWarps + kRotWarps;  // 8
-constexpr int kMmaWarp = kProducerWarp + 1;               // 9
-constexpr int kThreads = (kMmaWarp + 1) * 32;             // 320
+constexpr int kMmaWarp = kProducerWarp + 1;               // 9: issues S = Q K^T
+constexpr int kMmaPvWarp = kMmaWarp + 1;                  // 10: issues O_tile = P V
+constexpr int kThreads = (kMmaPvWarp + 1) * 32;           // 352
 constexpr int kRotThreads = kRotWarps * 32;
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 
@@ -645,11 +646,11 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
             if (!ok) report_timeout(a);
         }
     } else if (warp == kMmaWarp) {
-        // ======================= MMA issuer =======================
+        // ======================= MMA issuer: S =======================
         if (lane == 0) {
             bool ok = mbar_wait(q_ready, 0);
             tc_fence_after();
-            const uint32_t t_s = tmem + kColS, t_ot = tmem + kColOT, t_p = tmem + kColP;
+            const uint32_t t_s = tmem + kColS;
             const uint32_t qh_addr = smem_addr(q_parts);
             // S(j), 16 dims per k-step kk (dim block kk / 4, 32 bytes per step within the row).
             auto issue_s = [&](int j) {
@@ -667,23 +668,25 @@ __global__ void __launch_bounds__(kThreads, 1) chunked_kernel(const __grid_const
                 tc_commit(s_full);
                 tc_commit(&kempty[j % kStages]);
             };
-            if (ok && n_tiles > 0) {
-                if (mbar_wait(&krot[0], 0)) {
-                    tc_fence_after();
-                    issue_s(0);
-                } else {
-                    ok = false;
-                }
-            }
+            // S(j) once K(j) is rotated and the softmax has read S(j-1).  The P.V
+            // products are issued by the next warp, so the two streams of MMAs
+            // overlap their issue.
             for (int j = 0; j < n_tiles && ok; ++j) {
-                if (j + 1 < n_tiles) {
-                    if (!mbar_wait(&krot[(j + 1) % kStages], ((j + 1) / kStages) & 1) || !mbar_wait(s_free, j & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    issue_s(j + 1);
+                if (!mbar_wait(&krot[j % kStages], (j / kStages) & 1) || (j > 0 && !mbar_wait(s_free, (j - 1) & 1))) {
+                    ok = false;
+                    break;
                 }
+                tc_fence_after();
+                issue_s(j);
+            }
+            if (!ok) report_timeout(a);
+        }
+    } else if (warp == kMmaPvWarp) {
+        // ======================= MMA issuer: P.V =======================
+        if (lane == 0) {
+            bool ok = true;
+            const uint32_t t_ot = tmem + kColOT, t_p = tmem + kColP;
+            for (int j = 0; j < n_tiles && ok; ++j) {
                 const int st = j % kStages;
                 if (!mbar_wait(p_full, j & 1) || !mbar_wait(&vfull[st], (j / kStages) & 1)) {
                     ok = false;
