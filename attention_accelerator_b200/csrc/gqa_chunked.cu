@@ -28,7 +28,10 @@
 // (O = O * 2^(m_old - m_new) + O_tile), which also makes the online-softmax
 // rescale exact.
 //
-// One CTA per (sequence, Q head): M = 128 query rows (TMEM lanes).
+// One CTA per (sequence, Q head) unit: M = 128 query rows (TMEM lanes).  The
+// units of the last, partly filled wave are split along the keys (a CTA then
+// takes a range of tiles and writes FP32 partial rows that chunk_combine_kernel
+// merges), so that the wave is filled.
 //   warps 0-3   softmax: thread r owns query row r.  Prologue: Q row r rotated
 //               at its position, scaled by scale*log2(e), split, stored to
 //               shared memory (A operand of S).  Per 48-key tile: S row from
@@ -40,11 +43,13 @@
 //               positions and write the three parts to rows 0-47 / 48-95 /
 //               96-143 (B operand of S).
 //   warp 8      TMA producer (2-stage rings of K and V tiles), TMEM allocator.
-//   warp 9      MMA issuer (one thread).  tcgen05.mma costs about 65 SM cycles
-//               to issue whatever its size, so every instruction here is as
-//               large as TMEM allows (N = 144/96/48 for S, 128 for O); the
-//               48-key tile is what fits three S blocks, the tile and running
-//               O and three P parts in the 512 TMEM columns.
+//   warp 9      S issuer and warp 10 P.V issuer (one thread each).
+//               tcgen05.mma costs about 65 SM cycles of the issuing thread
+//               whatever its size, so every instruction is as large as TMEM
+//               allows (N = 144/96/48 for S, 128 for O) and the two streams
+//               come from two threads; the 48-key tile is what fits three S
+//               blocks, the tile and running O and three P parts in the 512
+//               TMEM columns.
 #include "gqa_device.cuh"
 #include "gqa_internal.h"
 
