@@ -36,7 +36,10 @@
 //               round trip.
 // Both kernels are launched with programmatic dependent launch: everything that
 // reads only the argument block (barrier set-up, RoPE tables) runs before
-// griddepcontrol.wait, overlapping the tail of the previous kernel in the stream.
+// griddepcontrol.wait, overlapping the tail of the previous kernel in the
+// stream; a single sequence's split also prefetches its Q rows and first K/V
+// tiles into L2 there.  A batch's CTAs take every sequence's full-chunk splits
+// first and the shorter last splits after them, so that those fill the last wave.
 #include "gqa_b200.h"
 #include "gqa_device.cuh"
 #include "gqa_internal.h"
