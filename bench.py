@@ -246,6 +246,9 @@ class RaggedBatch(Workload):
         self.v = [torch.randn((total, 8, 128), generator=g, device=device).to(torch.bfloat16)
                   for _ in range(self.nsets)]
         self.plan = gqa.plan_batch(self.seq, device=device)
+        # decode_kernel, plus split_merge_kernel when some sequence has several splits
+        self.launches_per_step = 2 if gqa.decode_plan(plan=self.plan).splits > batch else 1
+        self.graph_ok = True  # no collective inside the step
         self.out = torch.empty((batch, 32, 128), dtype=torch.bfloat16, device=device)
         self.l2_note = f"{self.nsets} rotating buffer sets of {per_set / 2**20:.0f} MiB"
 
@@ -419,6 +422,17 @@ class ChunkedDecode(Workload):
                   for _ in range(self.nsets)]
         self.out = torch.empty((self.local, n_queries, 32, 128), dtype=torch.bfloat16, device=device)
         self.l2_note = f"{self.nsets} rotating buffer sets of {per_set / 2**20:.0f} MiB per rank"
+        # Two kernels per step when the last wave's units are split along the keys
+        # (chunked_kernel + chunk_combine_kernel): the split needs more than the
+        # 256-byte minimum workspace.
+        import ctypes
+        from attention_accelerator_b200 import _lib
+        from attention_accelerator_b200.api import make_params
+        p = make_params(seq_len=seq_len, query_position=seq_len - 1)
+        c = _lib.GqaChunkParams(batch=self.local, n_queries=n_queries, first_position=self.first)
+        need = _lib.load().gqa_chunked_workspace_bytes(ctypes.byref(p), ctypes.byref(c))
+        self.launches_per_step = 2 if need > _lib.CHUNKED_WORKSPACE_BYTES else 1
+        self.graph_ok = True  # no collective inside the step
 
     @property
     def sets(self):
