@@ -152,3 +152,18 @@ def test_plan_batch_descriptors_on_host():
     assert [d.kv_start for d in plan.host] == [0, 5, 14]
     assert [d.pos_end for d in plan.host] == [5, 9, 1]
     assert plan.device.numel() == 3 * 24
+
+
+def test_bench_reference_arm_json_line():
+    """`bench.py --impl reference` (the reference algorithm on the host cores) prints one
+    JSON line with the contract's keys; config 1 keeps it to a few seconds."""
+    import json
+    import sys
+    res = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", "config1", "--steps", "2",
+                          "--warmup", "3"], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    line = json.loads([ln for ln in res.stdout.splitlines() if ln.startswith("{")][-1])
+    assert line["impl"] == "reference" and line["unit"] == "GB/s" and line["value"] > 0
+    assert line["metric"].startswith("decode-attn KV-read HBM GB/s")
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
