@@ -36,11 +36,26 @@ def is_stale() -> bool:
 
 
 def build_library(force: bool = False, verbose: bool = False) -> Path:
-    """Compile ``lib/libgqa_b200.so`` for sm_100a if it is missing or older than its sources."""
+    """Compile ``lib/libgqa_b200.so`` for sm_100a if it is missing or older than its sources.
+
+    Processes that call this at the same time (the ranks of a torchrun job)
+    serialise on a lock file: one compiles, the others then find it fresh."""
     if not force and not is_stale():
         return LIB
     LIB.parent.mkdir(parents=True, exist_ok=True)
-    tmp = LIB.with_suffix(".so.tmp")
+    import fcntl
+    with open(LIB.parent / ".build.lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        try:
+            if not force and not is_stale():
+                return LIB
+            return _compile(verbose)
+        finally:
+            fcntl.flock(lock, fcntl.LOCK_UN)
+
+
+def _compile(verbose: bool) -> Path:
+    tmp = LIB.with_suffix(f".so.tmp{os.getpid()}")
     cmd = [nvcc_path(), "-shared", "-Xcompiler", "-fPIC", "-O3", "-std=c++17", *ARCH_FLAGS, "-lineinfo",
            f"-I{INCLUDE}", f"-I{CSRC}", "-o", str(tmp), *map(str, SOURCES)]
     if verbose:
