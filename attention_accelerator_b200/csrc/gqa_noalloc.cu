@@ -57,7 +57,9 @@ extern "C" int gqa_decode_noalloc(const void* q, const void* k, const void* v, v
     const int sst = scratch_for_current_device(&scratch);
     if (sst != GQA_OK) return sst;
     // The split table and partials are written before they are read within a
-    // call, and the status word starts at zero (device variables are
-    // zero-initialised when the library loads), so nothing needs clearing.
+    // call.  The only state that must start at zero, the per-KV-head split
+    // arrival counters, is zero when the library loads (device variables are
+    // zero-initialised) and the last split of each head sets its counter back
+    // to zero before the kernel ends, so nothing needs clearing between calls.
     return gqa_decode(q, k, v, out, p, scratch, kScratchBytes, stream);
 }
