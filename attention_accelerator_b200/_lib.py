@@ -29,6 +29,7 @@ GQA_ERR_DEVICE_TIMEOUT = 14
 GQA_ERR_UNSUPPORTED_DEVICE = 15
 GQA_ERR_ROPE_THETA = 16
 GQA_ERR_FLAGS = 17
+GQA_ERR_MEMORY = 18
 
 #: codes that describe a bad call configuration (the reference's config_error)
 CONFIG_ERRORS = {GQA_ERR_GEOMETRY, GQA_ERR_SEQ_LEN, GQA_ERR_N_KV_TILES, GQA_ERR_SCALE,

@@ -121,6 +121,21 @@ def _to_device(t: torch.Tensor, device: torch.device) -> torch.Tensor:
     return t.to(device, non_blocking=t.is_pinned())
 
 
+def _check_out(out: torch.Tensor, shape: tuple, dtype: torch.dtype, device: torch.device) -> None:
+    """A caller-supplied output must hold every row the kernel writes: the kernels
+    write through the pointer and strides they are given, so a smaller tensor would
+    be written past its end."""
+    if tuple(out.shape) != tuple(shape) or out.dtype != dtype or out.stride(-1) != 1 or out.device != device:
+        raise ValueError(f"out must be {dtype} {list(shape)} on {device} with a contiguous last dim, "
+                         f"got {out.dtype} {list(out.shape)} on {out.device}")
+
+
+def _check_cuda(device: torch.device, **tensors: torch.Tensor) -> None:
+    for name, t in tensors.items():
+        if t.device != device:
+            raise ValueError(f"{name} is on {t.device}; every tensor of this call must be on {device}")
+
+
 def _set_q_out(p: GqaParams, q: torch.Tensor, out: torch.Tensor, partial: bool) -> None:
     p.q_batch_stride = q.stride(0) if q.dim() == 3 else N_Q_HEADS * HEAD_DIM
     p.q_head_stride = q.stride(-2)
@@ -182,10 +197,17 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, seq_len: int | 
     p.v_pos_stride, p.v_head_stride, vrows = _kv_strides(v, layout)
     if rows < seq_len or vrows < seq_len:
         raise ValueError(f"K/V hold {min(rows, vrows)} rows, SEQ_LEN is {seq_len}")
+    _check_cuda(device, k=k, v=v)
+    if out is not None and out.is_cuda:
+        _check_out(out, (N_Q_HEADS, HEAD_DIM) if out.dim() == 2 else (1, N_Q_HEADS, HEAD_DIM), torch.bfloat16, device)
     dev_out = out if (out is not None and out.is_cuda) else torch.empty(
         (N_Q_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=device)
     _set_q_out(p, q, dev_out, False)
     if mask_out is not None:
+        need = p.n_kv_tiles * p.kv_block_len
+        if mask_out.dtype != torch.uint8 or mask_out.device != device or not mask_out.is_contiguous() \
+                or mask_out.numel() < need:
+            raise ValueError(f"mask_out must be a contiguous uint8 tensor on {device} with >= {need} entries")
         p.mask_out = mask_out.data_ptr()
         p.mask_stride = mask_out.shape[-1]
     stream = _stream_ptr(device)
@@ -234,8 +256,12 @@ def decode_chunked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, first_p
     p.k_pos_stride, p.k_head_stride = k.stride(rows_dim), k.stride(head_dim_idx)
     p.v_pos_stride, p.v_head_stride = v.stride(rows_dim), v.stride(head_dim_idx)
     device = q.device
+    if device.type != "cuda":
+        raise ValueError("decode_chunked takes CUDA tensors")
+    _check_cuda(device, k=k, v=v)
     if out is None:
         out = torch.empty((batch, n, N_Q_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=device)
+    _check_out(out, (batch, n, N_Q_HEADS, HEAD_DIM), torch.bfloat16, device)
     p.q_batch_stride, p.q_head_stride = q.stride(0), q.stride(2)
     p.out_batch_stride, p.out_head_stride = out.stride(0), out.stride(2)
     c = _lib.GqaChunkParams(batch=batch, n_queries=n, first_position=first_position, reserved=0,
@@ -349,9 +375,14 @@ def decode_batch(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, plan: BatchP
         if d.kv_start + max(0, hi - d.pos_begin) > min(k_rows, v_rows):
             raise ValueError(f"sequence {i}: its keys end at stored row "
                              f"{d.kv_start + hi - d.pos_begin}, K/V hold {min(k_rows, v_rows)} rows")
+    if device.type != "cuda":
+        raise ValueError("decode_batch takes CUDA tensors")
+    _check_cuda(device, k=k, v=v, plan=plan.device)
+    shape = (plan.batch, N_Q_HEADS, PARTIAL_FLOATS if plan.partial else HEAD_DIM)
+    dtype = torch.float32 if plan.partial else torch.bfloat16
     if out is None:
-        shape = (plan.batch, N_Q_HEADS, PARTIAL_FLOATS if plan.partial else HEAD_DIM)
-        out = torch.empty(shape, dtype=torch.float32 if plan.partial else torch.bfloat16, device=device)
+        out = torch.empty(shape, dtype=dtype, device=device)
+    _check_out(out, shape, dtype, device)
     _set_q_out(p, q, out, plan.partial)
     stream = _stream_ptr(device)
     nbytes = lib.gqa_workspace_bytes(ctypes.byref(p), plan.host, plan.batch)
@@ -373,8 +404,11 @@ def combine_partials(parts: torch.Tensor, out: torch.Tensor | None = None) -> to
             or parts.shape[-2] != N_Q_HEADS or parts.stride(-1) != 1 or parts.stride(-2) != PARTIAL_FLOATS:
         raise ValueError("parts must be float32 [n_parts, B, 32, 132] with contiguous rows")
     n, b = parts.shape[0], parts.shape[1]
+    if parts.device.type != "cuda":
+        raise ValueError("combine_partials takes CUDA tensors")
     if out is None:
         out = torch.empty((b, N_Q_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=parts.device)
+    _check_out(out, (b, N_Q_HEADS, HEAD_DIM), torch.bfloat16, parts.device)
     _check(lib.gqa_combine_partials(parts.data_ptr(), n, parts.stride(0), parts.stride(1), b, out.data_ptr(),
                                     out.stride(0), out.stride(1), _stream_ptr(parts.device)), "combine_partials")
     return out
@@ -383,8 +417,8 @@ def combine_partials(parts: torch.Tensor, out: torch.Tensor | None = None) -> to
 def rope_rows(x: torch.Tensor, positions: torch.Tensor, rope_theta: float = ROPE_THETA) -> torch.Tensor:
     """RoPE of BF16 rows ``[rows, 128]`` at int32 ``positions`` -> FP32 rows (device code of the kernels)."""
     lib = _lib.load()
-    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != HEAD_DIM or not x.is_contiguous():
-        raise ValueError("x must be contiguous bfloat16 [rows, 128]")
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != HEAD_DIM or not x.is_contiguous() or not x.is_cuda:
+        raise ValueError("x must be a contiguous bfloat16 CUDA tensor [rows, 128]")
     positions = positions.to(device=x.device, dtype=torch.int32).contiguous()
     out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
     _check(lib.gqa_rope_rows(x.data_ptr(), positions.data_ptr(), out.data_ptr(), x.shape[0], rope_theta,
@@ -408,8 +442,8 @@ def rope_k_cache(k: torch.Tensor, positions: torch.Tensor, *, layout: str = "pos
         raise ValueError(f"{positions.numel()} positions for {n} stored rows")
     if out is None:
         out = torch.empty_like(k)
-    if out.shape != k.shape or out.stride() != k.stride() or out.dtype != torch.bfloat16:
-        raise ValueError("out must match k's shape, strides and dtype")
+    if out.shape != k.shape or out.stride() != k.stride() or out.dtype != torch.bfloat16 or out.device != k.device:
+        raise ValueError("out must match k's shape, strides, dtype and device")
     _check(lib.gqa_rope_k_cache(k.data_ptr(), out.data_ptr(), positions.data_ptr(), n, pos_stride, head_stride,
                                 rope_theta, _stream_ptr(k.device)), "rope_k_cache")
     return out
@@ -453,6 +487,8 @@ def rope_rtl(x: torch.Tensor, positions: torch.Tensor, *, layout: str = "positio
     phase, sincos = _rtl_rom_tables(x.device, rope_theta, rom_addr_bits)
     if out is None:
         out = torch.empty_like(x)
+    if out.shape != x.shape or out.stride() != x.stride() or out.dtype != torch.bfloat16 or out.device != x.device:
+        raise ValueError("out must match x's shape, strides, dtype and device")  # written with x's strides
     _check(lib.gqa_rope_rtl(x.data_ptr(), out.data_ptr(), positions.data_ptr(), n, heads, pos_stride, head_stride,
                             phase.data_ptr(), sincos.data_ptr(), rom_addr_bits, _stream_ptr(x.device)), "rope_rtl")
     return out

@@ -17,6 +17,26 @@
 static_assert(sizeof(gqa_seq_desc) == sizeof(gqa::SeqDesc), "descriptor layout");
 static_assert(sizeof(gqa_partial_row) == gqa::kPartialFloats * sizeof(float), "partial row layout");
 
+namespace gqa {
+
+int check_device_memory(std::initializer_list<const void*> ptrs) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return GQA_ERR_CUDA;
+    for (const void* ptr : ptrs) {
+        if (ptr == nullptr) continue;  // each entry point checks its required pointers itself
+        cudaPointerAttributes at;
+        if (cudaPointerGetAttributes(&at, ptr) != cudaSuccess) {
+            (void)cudaGetLastError();  // leave no error behind for the launch checks that follow
+            return GQA_ERR_MEMORY;
+        }
+        if (at.type == cudaMemoryTypeManaged) continue;
+        if (at.type != cudaMemoryTypeDevice || at.device != dev) return GQA_ERR_MEMORY;
+    }
+    return GQA_OK;
+}
+
+}  // namespace gqa
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -188,7 +208,7 @@ int check_layout(const void* q, const void* k, const void* v, const void* out, c
     } else if (!stride_ok(p->out_head_stride) || !stride_ok(p->out_batch_stride)) {
         return GQA_ERR_ALIGNMENT;  // BF16 rows are written 4 elements at a time
     }
-    return GQA_OK;
+    return gqa::check_device_memory({q, k, v, out, p->mask_out});
 }
 
 int check_desc(const gqa::SeqDesc& d, bool need_keys) {
@@ -404,6 +424,7 @@ const char* gqa_status_string(int status) {
         case GQA_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 GPU";
         case GQA_ERR_ROPE_THETA: return "invalid rope_theta, or more than 4 distinct rope_theta values on one device";
         case GQA_ERR_FLAGS: return "gqa_params.flags holds a bit this entry point does not support";
+        case GQA_ERR_MEMORY: return "a tensor, table or workspace pointer is not memory of the current GPU";
         default: return "unknown status";
     }
 }
@@ -492,6 +513,8 @@ int gqa_decode(const void* q, const void* k, const void* v, void* out, const gqa
     const gqa::SeqDesc d = single_desc(p);
     const Plan pl = make_plan(&d, 1, sms, true);
     if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
+    st = gqa::check_device_memory({workspace});
+    if (st != GQA_OK) return st;
     gqa::DecodeArgs a;
     st = fill_args(a, q, k, v, out, p, workspace, pl, 1);
     if (st != GQA_OK) return st;
@@ -528,6 +551,8 @@ int gqa_decode_batched(const void* q, const void* k, const void* v, void* out, c
     // sequence plan: splits merged in-kernel, no split-merge launch.
     const Plan pl = make_plan(d, batch, sms, batch == 1);
     if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
+    st = gqa::check_device_memory({workspace, dev_descs});
+    if (st != GQA_OK) return st;
     gqa::DecodeArgs a;
     st = fill_args(a, q, k, v, out, p, workspace, pl, batch);
     if (st != GQA_OK) return st;
@@ -561,6 +586,8 @@ int gqa_decode_exchange(const void* q, const void* k, const void* v, void* out, 
     if (st != GQA_OK) return st;
     const Plan pl = make_plan(&d, 1, sms, true, false);  // single-sequence plan, no clusters
     if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
+    st = gqa::check_device_memory({workspace, peer_buffers});  // the array of bases; peers are not local memory
+    if (st != GQA_OK) return st;
     gqa::DecodeArgs a;
     st = fill_args(a, q, k, v, out, p, workspace, pl, 1);
     if (st != GQA_OK) return st;
@@ -583,7 +610,9 @@ int gqa_combine_partials(const float* partials, int n_parts, int64_t part_stride
     if (n_parts < 1 || batch < 1) return GQA_ERR_BATCH;
     if (part_stride < 0 || batch_stride < 0 || out_batch_stride < 0 || out_head_stride < 0) return GQA_ERR_ALIGNMENT;
     int sms = 0;
-    const int st = current_device(&sms);
+    int st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    st = gqa::check_device_memory({partials, out});
     if (st != GQA_OK) return st;
     if (gqa::launch_combine(partials, n_parts, part_stride, batch_stride, batch, out, out_batch_stride,
                             out_head_stride, static_cast<cudaStream_t>(stream)) != cudaSuccess)
@@ -609,6 +638,8 @@ int gqa_decode_chunked(const void* q, const void* k, const void* v, void* out, c
         !stride_ok(c->v_batch_stride))
         return GQA_ERR_ALIGNMENT;
     if (!workspace || !aligned16(workspace) || workspace_bytes < GQA_CHUNKED_WORKSPACE_BYTES) return GQA_ERR_WORKSPACE;
+    st = gqa::check_device_memory({workspace});
+    if (st != GQA_OK) return st;
     int sms = 0;
     st = current_device(&sms);
     if (st != GQA_OK) return st;
@@ -670,7 +701,9 @@ int gqa_rope_rows(const void* x, const int32_t* positions, float* out, int rows,
     if (!(rope_theta > 0.f) || !std::isfinite(rope_theta)) return GQA_ERR_ROPE_THETA;
     if (rows == 0) return GQA_OK;
     int sms = 0;
-    const int st = current_device(&sms);
+    int st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    st = gqa::check_device_memory({x, positions, out});
     if (st != GQA_OK) return st;
     uint64_t step[gqa::kPairs];
     rope_steps((double)rope_theta, step, nullptr, nullptr, 0);
@@ -689,7 +722,9 @@ int gqa_rope_k_cache(const void* k, void* k_rot, const int32_t* positions, int n
     if (!(rope_theta > 0.f) || !std::isfinite(rope_theta)) return GQA_ERR_ROPE_THETA;
     if (n_positions == 0) return GQA_OK;
     int sms = 0;
-    const int st = current_device(&sms);
+    int st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    st = gqa::check_device_memory({k, k_rot, positions});
     if (st != GQA_OK) return st;
     uint64_t step[gqa::kPairs];
     rope_steps((double)rope_theta, step, nullptr, nullptr, 0);

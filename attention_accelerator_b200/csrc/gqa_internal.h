@@ -6,7 +6,16 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <initializer_list>
+
 namespace gqa {
+
+// GQA_OK when every non-null pointer is memory the current GPU's kernels and
+// TMA units address directly: a device allocation of this GPU or managed
+// memory.  Host memory (pageable or pinned) and another GPU's allocations give
+// GQA_ERR_MEMORY, before anything is launched, so that a wrong pointer at the C
+// boundary becomes a status instead of a memory fault on the GPU.
+int check_device_memory(std::initializer_list<const void*> ptrs);
 
 struct DecodeArgs;
 struct RopeTable;

@@ -544,6 +544,8 @@ int gqa_mem_decode(const void* text, size_t text_bytes, int elements, void* rows
     if (blocks && (!workspace || workspace_bytes < gqa_mem_decode_workspace_bytes(text_bytes)))
         return GQA_ERR_WORKSPACE;
     if (blocks > 0x7fffffffull) return GQA_ERR_BATCH;
+    const int st = gqa::check_device_memory({text, rows, result, blocks ? workspace : nullptr});
+    if (st != GQA_OK) return st;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (cudaMemsetAsync(result, 0, sizeof(gqa_mem_result), s) != cudaSuccess ||
         cudaMemsetAsync(&result->bad_offset, 0xff, sizeof(result->bad_offset), s) != cudaSuccess)
@@ -601,6 +603,8 @@ int gqa_mem_encode(const void* rows, uint64_t n_rows, int elements, void* text, 
     if (!n_rows) return GQA_OK;
     if (!rows || !text) return GQA_ERR_NULL_POINTER;
     if ((reinterpret_cast<uintptr_t>(text) & 15u) || (reinterpret_cast<uintptr_t>(rows) & 1u)) return GQA_ERR_ALIGNMENT;
+    const int st = gqa::check_device_memory({rows, text});
+    if (st != GQA_OK) return st;
     gqa::MemEncodeArgs a;
     a.rows = static_cast<const uint16_t*>(rows);
     a.n_rows = n_rows;

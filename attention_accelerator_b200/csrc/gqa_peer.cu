@@ -202,6 +202,8 @@ int gqa_combine_peers(const float* partials, int64_t partial_batch_stride, const
     if (partial_batch_stride < (int64_t)gqa::kNumQHeads * gqa::kPartialFloats || out_batch_stride < 0 ||
         out_head_stride < 0)
         return GQA_ERR_ALIGNMENT;
+    const int st = gqa::check_device_memory({partials, peer_buffers, out, workspace});  // peer_buffers: the array
+    if (st != GQA_OK) return st;
     if (gqa::launch_combine_peers(partials, partial_batch_stride, reinterpret_cast<const uint64_t*>(peer_buffers), world,
                                   rank, batch, out, out_batch_stride, out_head_stride,
                                   static_cast<uint32_t*>(workspace), static_cast<cudaStream_t>(stream)) != cudaSuccess)

@@ -15,6 +15,7 @@
 // One warp per row; lane l owns pairs 2l and 2l+1.
 #include "gqa_b200.h"
 #include "gqa_device.cuh"
+#include "gqa_internal.h"
 
 namespace gqa {
 
@@ -68,6 +69,8 @@ extern "C" int gqa_rope_rtl(const void* x, void* out, const int32_t* positions, 
     const int64_t rows = (int64_t)n_positions * heads;
     if (rows == 0) return GQA_OK;
     if (rows > 0x7fffffffLL) return GQA_ERR_BATCH;
+    const int st = gqa::check_device_memory({x, out, positions, phase_rom, sincos_rom});
+    if (st != GQA_OK) return st;
     gqa::rope_rtl_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), positions, (int)rows, heads,
         pos_stride, head_stride, phase_rom, sincos_rom, rom_addr_bits);

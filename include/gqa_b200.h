@@ -13,7 +13,12 @@
  * Everything here is plain C: pointers, sizes and a `void*` CUDA stream handle
  * (a cudaStream_t; NULL is the legacy default stream).  BF16 tensors are passed
  * as `const void*` to 2-byte BF16 codes.  All device pointers must be 16-byte
- * aligned and every stride (in elements) a multiple of 8.  Calls are
+ * aligned and every stride (in elements) a multiple of 8.  Tensor, table,
+ * descriptor and workspace pointers must be memory of the current GPU (a
+ * device allocation or managed memory); host memory, pinned or not, and
+ * another GPU's allocations are refused with GQA_ERR_MEMORY before anything is
+ * launched.  (The NVLink exchange's peer buffers are the exception: they are
+ * reached through a device array of their addresses.)  Calls are
  * asynchronous on `stream` and re-entrant across streams as long as each
  * concurrent call has its own workspace.
  *
@@ -51,7 +56,9 @@ enum gqa_status {
     GQA_ERR_DEVICE_TIMEOUT = 14,   /* a bounded wait inside a kernel gave up (see gqa_read_status) */
     GQA_ERR_UNSUPPORTED_DEVICE = 15, /* current device is not sm_100 */
     GQA_ERR_ROPE_THETA = 16,       /* rope_theta <= 0, not finite, or a 5th distinct value on one device */
-    GQA_ERR_FLAGS = 17             /* gqa_params.flags holds a bit this entry point does not know */
+    GQA_ERR_FLAGS = 17,            /* gqa_params.flags holds a bit this entry point does not know */
+    GQA_ERR_MEMORY = 18            /* a tensor, table or workspace pointer is not memory of the current
+                                      GPU (host memory, pageable or pinned, or another GPU's memory) */
 };
 
 /* GQA_FLAG_* values for gqa_params.flags. */

@@ -46,6 +46,41 @@ def test_library_exports_every_declared_symbol():
     assert set(declared_functions()) <= exported
 
 
+def test_status_codes_match_header():
+    """Every GQA_ERR_* value of the header's enum is the binding's, and has its own message."""
+    codes = dict((n, int(v)) for n, v in re.findall(r"\b(GQA_ERR_\w+)\s*=\s*(\d+)", HEADER.read_text()))
+    assert codes and codes["GQA_ERR_MEMORY"] == 18
+    for name, value in codes.items():
+        assert getattr(_lib, name) == value, name
+    messages = {_lib.status_string(v) for v in codes.values()}
+    assert len(messages) == len(codes) and "unknown status" not in messages
+
+
+def test_api_refuses_host_tensors_and_wrong_outputs_before_any_call():
+    """Paths with no host-buffer support refuse CPU tensors, and a caller's ``out``
+    must hold every row the kernel writes; both are checked in Python, before the
+    library is called."""
+    import torch
+    from attention_accelerator_b200 import api
+    q = torch.zeros((1, 2, 32, 128), dtype=torch.bfloat16)
+    kv = torch.zeros((1, 64, 8, 128), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        gqa.decode_chunked(q, kv, kv, first_position=62)
+    plan = gqa.plan_batch([64], device=torch.device("cpu"))
+    with pytest.raises(ValueError, match="CUDA"):
+        gqa.decode_batch(q[:, 0], kv[0], kv[0], plan)
+    with pytest.raises(ValueError, match="CUDA"):
+        gqa.combine_partials(torch.zeros((2, 1, 32, 132)))
+    with pytest.raises(ValueError, match="CUDA"):
+        gqa.rope_rows(torch.zeros((4, 128), dtype=torch.bfloat16), torch.arange(4))
+    out = torch.empty((32, 128), dtype=torch.bfloat16)
+    api._check_out(out, (32, 128), torch.bfloat16, torch.device("cpu"))
+    for bad in (torch.empty((16, 128), dtype=torch.bfloat16), torch.empty((32, 128)),
+                torch.empty((128, 32), dtype=torch.bfloat16).t()):
+        with pytest.raises(ValueError, match="out must be"):
+            api._check_out(bad, (32, 128), torch.bfloat16, torch.device("cpu"))
+
+
 def test_struct_layouts():
     assert ctypes.sizeof(_lib.GqaSeqDesc) == 24
     assert ctypes.sizeof(_lib.GqaParams) == 12 * 4 + 8 * 8 + 8 + 8
