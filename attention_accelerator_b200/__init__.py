@@ -2,10 +2,10 @@
 
 Public API (see ``api``): :func:`decode`, :func:`plan_batch` + :func:`decode_batch`,
 :func:`decode_chunked`, :func:`combine_partials`, :func:`decode_plan`, :func:`rope_rows`, :func:`rope_k_cache`,
-:func:`rope_phase_rom`,
-:func:`rope_sincos_rom`, :func:`validate`, :func:`read_device_status`.
-All compute runs in ``lib/libgqa_b200.so`` through the C ABI of
-``include/gqa_b200.h``.
+:func:`rope_rtl`, :func:`rope_phase_rom`, :func:`rope_sincos_rom`, :func:`validate`,
+:func:`read_device_status`; the ``.mem`` codec in ``memfile``; the multi-GPU
+long-context exchange in ``distributed``.  All compute runs in
+``lib/libgqa_b200.so`` through the C ABI of ``include/gqa_b200.h``.
 """
 from .api import (DEFAULT_KV_BLOCK_LEN, GROUP_SIZE, HEAD_DIM, N_KV_HEADS, N_Q_HEADS, ROPE_THETA, TILE_DIM,
                   BatchPlan, GqaConfigError, GqaError, SplitPlan, combine_partials, decode, decode_batch, decode_chunked,
