@@ -87,31 +87,45 @@ class PeerExchange:
         if st != _lib.GQA_OK:
             raise RuntimeError(f"gqa_peer_buffer_create: {_lib.status_string(st)}")
         self._own = own.value
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
         self._opened = []
-        ptrs = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(self._own)
-                continue
-            p = ctypes.c_void_p()
-            hb = (ctypes.c_ubyte * _lib.PEER_HANDLE_BYTES).from_buffer_copy(h)
-            st = lib.gqa_peer_buffer_open(hb, ctypes.byref(p))
-            if st != _lib.GQA_OK:
-                raise RuntimeError(f"gqa_peer_buffer_open(rank {r}): {_lib.status_string(st)}")
-            self._opened.append(p.value)
-            ptrs.append(p.value)
-        self.bases = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
-        self.status = torch.zeros(64, dtype=torch.int32, device=self.device)
-        dist.barrier(group)
+        try:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            ptrs = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                hb = (ctypes.c_ubyte * _lib.PEER_HANDLE_BYTES).from_buffer_copy(h)
+                st = lib.gqa_peer_buffer_open(hb, ctypes.byref(p))
+                if st != _lib.GQA_OK:
+                    raise RuntimeError(f"gqa_peer_buffer_open(rank {r}): {_lib.status_string(st)}")
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            self.bases = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+            self.status = torch.zeros(64, dtype=torch.int32, device=self.device)
+            dist.barrier(group)
+        except BaseException:
+            # A peer's handle did not open or a collective failed (e.g. a rank is
+            # gone): release what this rank holds; nothing has been launched yet.
+            for p in self._opened:
+                lib.gqa_peer_buffer_close(p)
+            self._opened = []
+            lib.gqa_peer_buffer_destroy(self._own)
+            self._own = None
+            raise
 
     def combine(self, partials: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """This rank's partials ``[batch, 32, 132]`` (FP32, CUDA) -> merged BF16 ``[batch, 32, 128]``."""
-        if partials.shape != (self.batch, 32, _lib.PARTIAL_FLOATS) or partials.dtype != torch.float32:
-            raise ValueError(f"partials must be float32 [{self.batch}, 32, {_lib.PARTIAL_FLOATS}]")
+        from . import api
+        if partials.shape != (self.batch, 32, _lib.PARTIAL_FLOATS) or partials.dtype != torch.float32 \
+                or partials.stride(-1) != 1 or partials.stride(-2) != _lib.PARTIAL_FLOATS or not partials.is_cuda:
+            raise ValueError(f"partials must be CUDA float32 [{self.batch}, 32, {_lib.PARTIAL_FLOATS}] "
+                             "with contiguous rows")
         if out is None:
             out = torch.empty((self.batch, 32, 128), dtype=torch.bfloat16, device=partials.device)
+        api._check_out(out, (self.batch, 32, 128), torch.bfloat16, partials.device)
         stream = torch.cuda.current_stream(partials.device).cuda_stream
         st = self.lib.gqa_combine_peers(partials.data_ptr(), partials.stride(0), self.bases.data_ptr(), self.world,
                                         self.rank, self.batch, out.data_ptr(), out.stride(0), out.stride(1),
@@ -134,6 +148,9 @@ class PeerExchange:
         from . import api
         if self.batch != 1 or plan.batch != 1 or plan.partial:
             raise ValueError("decode() exchanges one sequence: PeerExchange(1) and a plan of one, partial=False")
+        if tuple(q.shape) != (1, 32, 128) or q.dtype != torch.bfloat16 or q.stride(-1) != 1 or not q.is_cuda:
+            raise ValueError("q must be a CUDA bfloat16 [1, 32, 128] with a contiguous last dim")
+        api._check_cuda(q.device, k=k, v=v, plan=plan.device)
         p = api.make_params(seq_len=1, scale=scale, rope_theta=api.ROPE_THETA if rope_theta is None else rope_theta)
         if k_rotated:  # pre-rotated K cache (api.rope_k_cache)
             p.flags |= _lib.GQA_FLAG_K_ROTATED
@@ -141,6 +158,7 @@ class PeerExchange:
         p.v_pos_stride, p.v_head_stride, _ = api._kv_strides(v, layout)
         if out is None:
             out = torch.empty((1, 32, 128), dtype=torch.bfloat16, device=q.device)
+        api._check_out(out, (1, 32, 128), torch.bfloat16, q.device)
         api._set_q_out(p, q, out, False)
         stream = torch.cuda.current_stream(q.device).cuda_stream
         nbytes = self.lib.gqa_workspace_bytes(ctypes.byref(p), plan.host, 1)

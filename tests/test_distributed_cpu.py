@@ -93,3 +93,73 @@ def test_balance_sequences_covers_and_balances():
         assert max(loads) - min(loads) <= max(lens)
     with pytest.raises(ValueError):
         shard_range(10, 2, 2)
+
+
+class _FakePeerLib:
+    """Stands in for the library's CUDA IPC buffer calls on CPU: it records what
+    PeerExchange creates, opens, closes and destroys; on ``fail_rank`` opening a
+    peer's handle fails, as it would for a peer whose process has gone."""
+
+    def __init__(self, rank: int, fail_rank: int):
+        self.rank, self.fail_rank, self.log = rank, fail_rank, []
+
+    def gqa_peer_buffer_bytes(self, batch):
+        return 4096
+
+    def gqa_peer_buffer_create(self, nbytes, ptr_ref, handle):
+        ptr_ref._obj.value = 0x10000 * (self.rank + 1)
+        handle[0] = self.rank
+        self.log.append(("create", ptr_ref._obj.value))
+        return 0
+
+    def gqa_peer_buffer_open(self, handle, ptr_ref):
+        if self.rank == self.fail_rank:
+            return 13  # GQA_ERR_CUDA
+        ptr_ref._obj.value = 0x10000 * (handle[0] + 1) + 0x100
+        self.log.append(("open", ptr_ref._obj.value))
+        return 0
+
+    def gqa_peer_buffer_close(self, ptr):
+        self.log.append(("close", ptr))
+
+    def gqa_peer_buffer_destroy(self, ptr):
+        self.log.append(("destroy", ptr))
+
+    def gqa_status_string(self, code):
+        return b"CUDA runtime error"
+
+
+def _peer_failure_worker(rank: int, port: int, result_q):
+    from datetime import timedelta
+
+    from attention_accelerator_b200 import _lib, distributed
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=timedelta(seconds=5))
+    fake = _FakePeerLib(rank, fail_rank=1)
+    _lib.load = lambda: fake
+    try:
+        distributed.PeerExchange(1, device=torch.device("cpu"))
+        result_q.put((rank, "constructed", fake.log))
+    except Exception as e:  # rank 1: its open failed; rank 0: its barrier timed out
+        result_q.put((rank, type(e).__name__, fake.log))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_releases_its_buffers_when_set_up_fails():
+    """Rank 1 cannot open rank 0's handle and raises; rank 0 opened rank 1's and
+    then waits at the set-up barrier until the process group's timeout.  Both
+    ranks must unmap what they opened and free their own buffer."""
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_failure_worker, args=(r, port, result_q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict((r, (what, log)) for r, what, log in (result_q.get(timeout=120) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1][0] == "RuntimeError"
+    assert results[1][1] == [("create", 0x20000), ("destroy", 0x20000)]
+    assert results[0][0] != "constructed"
+    assert results[0][1] == [("create", 0x10000), ("open", 0x20100), ("close", 0x20100), ("destroy", 0x10000)]
