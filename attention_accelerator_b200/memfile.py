@@ -92,7 +92,10 @@ def decode_mem(data, elements: int, device=None):
         raise RuntimeError(f"gqa_mem_decode: {_lib.status_string(st)}")
     n_rows, bad = (int(x) for x in result.cpu())
     if bad != -1:  # UINT64_MAX read as int64
-        line = int((text[:bad] == ord("\n")).sum()) + 1
+        # line ends as the parser reads them: '\n', '\r\n', or a '\r' alone
+        head = text[:min(bad + 1, n)].cpu().numpy()
+        nxt = np.append(head[1:bad + 1], 0)[:bad]
+        line = int(((head[:bad] == 10) | ((head[:bad] == 13) & (nxt != 10))).sum()) + 1
         raise ValueError(f"line {line}: expected {4 * elements} hex digits (and '_'), "
                          f"surrounded by blanks only")
     if n_rows > max_rows:

@@ -120,6 +120,18 @@ def test_malformed_line_rejected_with_its_line_number(bad, cuda_device, tmp_path
         memfile.decode_mem(text.encode(), 16)
 
 
+@pytest.mark.parametrize("end", ["\r", "\r\n", "\n\r"])
+def test_malformed_line_number_with_other_line_ends(end, cuda_device, tmp_path):
+    """CR and CRLF line ends count one line each (a '\n\r' pair is two)."""
+    good = "0123456789abcdef" * 4
+    text = end.join([good, "// c", good, "0123", good]) + end
+    with pytest.raises(ValueError):
+        _oracle_decode(text.encode(), 16, tmp_path)
+    want = 4 if end != "\n\r" else 7
+    with pytest.raises(ValueError, match=rf"^line {want}:"):
+        memfile.decode_mem(text.encode(), 16)
+
+
 def host_encode(rows: np.ndarray) -> bytes:
     """Vectorised write_mem text for large arrays (the bytes of oracle.bf16.mem_text)."""
     hexd = np.frombuffer(b"0123456789abcdef", dtype=np.uint8)
