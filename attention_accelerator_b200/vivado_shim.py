@@ -42,7 +42,7 @@ def _fail(msg: str, code: int = 1) -> int:
 
 def main(argv: list[str] | None = None) -> int:
     from . import _lib
-    from .api import GqaConfigError, make_params
+    from .api import GqaConfigError, GqaError, make_params
     from .memfile import compare_rows, decode_mem, encode_mem, read_config
 
     vectors = Path(os.environ.get("VECTORS_DIR") or "tests/data").resolve()
@@ -56,9 +56,12 @@ def main(argv: list[str] | None = None) -> int:
     cfg = read_config(vectors / "gqa_config.txt")
     if "SEQ_LEN" not in cfg:
         return _fail("SEQ_LEN missing from gqa_config.txt")
-    seq_len = int(cfg["SEQ_LEN"])
-    kv_block_len = int(cfg.get("KV_BLOCK_LEN", 16))
-    qpos = int(cfg.get("QUERY_POSITION", seq_len - 1))
+    try:
+        seq_len = int(cfg["SEQ_LEN"])
+        kv_block_len = int(cfg.get("KV_BLOCK_LEN", 16))
+        qpos = int(cfg.get("QUERY_POSITION", seq_len - 1))
+    except ValueError as exc:
+        return _fail(f"gqa_config.txt: {exc}")
     build.mkdir(parents=True, exist_ok=True)
     out_path = build / "gqa_rtl_out.mem"
 
@@ -88,9 +91,14 @@ def main(argv: list[str] | None = None) -> int:
         except ValueError as exc:
             raise SystemExit(_fail(f"{vectors / name}: {exc}"))
 
-    q = load("gqa_q.mem", 16).view(torch.bfloat16).reshape(-1, 128)
-    k = load("gqa_k.mem", 16).view(torch.bfloat16).reshape(8, -1, 128)
-    v = load("gqa_v.mem", 16).view(torch.bfloat16).reshape(8, -1, 128)
+    q, k, v = (load(f"gqa_{n}.mem", 16).view(torch.bfloat16) for n in "qkv")
+    # transport beats of 16 elements: Q is 32 rows of 128, K and V are 8 heads x rows x 128
+    if q.numel() != 32 * 128:
+        return _fail(f"gqa_q.mem holds {q.numel()} elements, expected {32 * 128}")
+    for name, t in (("gqa_k.mem", k), ("gqa_v.mem", v)):
+        if t.numel() == 0 or t.numel() % (8 * 128):
+            return _fail(f"{name} holds {t.numel()} elements, not a whole number of 8 x 128-element rows")
+    q, k, v = q.reshape(32, 128), k.reshape(8, -1, 128), v.reshape(8, -1, 128)
     golden = load("gqa_golden.mem", 128).cpu().numpy().view(np.uint16)
     try:
         out = decode(q, k, v, seq_len=seq_len, query_position=qpos, kv_block_len=kv_block_len, layout="head_major",
@@ -98,6 +106,10 @@ def main(argv: list[str] | None = None) -> int:
     except GqaConfigError as exc:
         print(f"FAIL: configuration rejected: {exc}")
         return 1
+    except ValueError as exc:  # e.g. fewer stored K/V rows than SEQ_LEN
+        return _fail(str(exc))
+    except GqaError as exc:  # the library refused the call for another reason
+        return _fail(str(exc))
     out_rows = out.view(torch.int16)
     out_path.write_bytes(encode_mem(out_rows))  # the testbench's row format, encoded on the GPU
     rows = out_rows.cpu().numpy().view(np.uint16)
