@@ -636,6 +636,21 @@ def timed_graph_run(torch, wl, steps, warmup, stream, dist_on):
     return start.elapsed_time(end), (t0, t1)
 
 
+def traffic_for(workload: str, bytes_per_launch: float):
+    """DRAM bytes per launch from the committed ncu capture of this workload, or
+    None.  A capture is of one launch on one GPU; it applies only to a launch
+    with the same algorithmic bytes (not to one rank's shard of a split
+    sequence at N > 1, whose launch moves 1/N of them)."""
+    path = ROOT / "profiles" / f"traffic_{workload}.json"
+    if not path.is_file():
+        return None
+    rec = json.loads(path.read_text())
+    alg = float(rec.get("algorithmic_bytes_per_launch", -1))
+    if abs(alg - bytes_per_launch) > 1e-3 * bytes_per_launch:
+        return None
+    return rec.get("dram_bytes_per_launch")
+
+
 def e2e_run(torch, wl, steps, device):
     host = wl.e2e_inputs()
     wl.e2e_step(host)
@@ -879,10 +894,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(wl, args.cpu_budget)
 
-    traffic = None
-    tpath = ROOT / "profiles" / f"traffic_{wl.name}.json"
-    if tpath.is_file():
-        traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+    traffic = traffic_for(wl.name, per_gpu_bytes)
     if wl.bound == "tensor":
         tpeak, tkind = peak_bf16()
         per_gpu_flops = wl.flops_per_step if wl.scaling == "weak" else wl.flops_per_step / world

@@ -81,6 +81,14 @@ def test_api_refuses_host_tensors_and_wrong_outputs_before_any_call():
             api._check_out(bad, (32, 128), torch.bfloat16, torch.device("cpu"))
 
 
+def test_bench_traffic_applies_only_to_the_captured_launch():
+    import bench
+    assert bench.traffic_for("config4_decode_s131072", 536887296) == 541605632
+    assert bench.traffic_for("config4_decode_s131072", 536887296 / 4) is None  # a rank's shard at N=4
+    assert bench.traffic_for("config3_ragged_b64", 1237770240) == 1260021760
+    assert bench.traffic_for("no_such_workload", 1.0) is None
+
+
 def test_struct_layouts():
     assert ctypes.sizeof(_lib.GqaSeqDesc) == 24
     assert ctypes.sizeof(_lib.GqaParams) == 12 * 4 + 8 * 8 + 8 + 8
