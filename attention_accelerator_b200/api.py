@@ -86,6 +86,10 @@ def validate(**registers) -> None:
 # ---------------------------------------------------------------------------
 _ws_lock = threading.Lock()
 _ws: dict[tuple[int, int], torch.Tensor] = {}
+# Buffers replaced by a larger one stay allocated: a CUDA graph captured with an
+# earlier call still holds their device address and would otherwise write into
+# memory the allocator has handed to another tensor.
+_ws_retired: list[torch.Tensor] = []
 
 
 def _workspace(device: torch.device, stream_ptr: int, nbytes: int) -> torch.Tensor:
@@ -93,6 +97,8 @@ def _workspace(device: torch.device, stream_ptr: int, nbytes: int) -> torch.Tens
     with _ws_lock:
         buf = _ws.get(key)
         if buf is None or buf.numel() < nbytes:
+            if buf is not None:
+                _ws_retired.append(buf)
             buf = torch.zeros(max(nbytes, 4096), dtype=torch.uint8, device=device)
             _ws[key] = buf
         return buf

@@ -89,6 +89,21 @@ def test_bench_traffic_applies_only_to_the_captured_launch():
     assert bench.traffic_for("no_such_workload", 1.0) is None
 
 
+def test_workspace_grows_without_freeing_the_old_buffer():
+    """A larger call on the same stream gets a new workspace; the old one stays
+    allocated (a captured CUDA graph may still address it) and is not reused."""
+    import torch
+    from attention_accelerator_b200 import api
+    dev, stream = torch.device("cpu"), 0x5eed
+    small = api._workspace(dev, stream, 100)
+    assert api._workspace(dev, stream, 4096) is small  # fits: same buffer
+    big = api._workspace(dev, stream, 1 << 16)
+    assert big is not small and big.numel() >= 1 << 16 and int(big.sum()) == 0
+    assert any(b is small for b in api._ws_retired)
+    assert api._workspace(dev, stream, 100) is big
+    del api._ws[(None, stream)]
+
+
 def test_struct_layouts():
     assert ctypes.sizeof(_lib.GqaSeqDesc) == 24
     assert ctypes.sizeof(_lib.GqaParams) == 12 * 4 + 8 * 8 + 8 + 8
