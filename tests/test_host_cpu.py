@@ -104,6 +104,37 @@ def test_workspace_grows_without_freeing_the_old_buffer():
     del api._ws[(None, stream)]
 
 
+_NULL_PROBE = r"""
+import ctypes
+from attention_accelerator_b200 import _lib
+lib = _lib.load()
+def is_ptr(a):
+    return issubclass(a, (ctypes._Pointer, ctypes.c_void_p, ctypes.c_char_p))
+for name, (res, argtypes) in sorted(_lib._SIGNATURES.items()):
+    if not any(is_ptr(a) for a in argtypes) or res not in (ctypes.c_int, ctypes.c_size_t):
+        continue
+    args = [None if is_ptr(a) else (1.0 if a in (ctypes.c_float, ctypes.c_double) else 1) for a in argtypes]
+    print(name, getattr(lib, name)(*args), flush=True)
+"""
+
+
+def test_every_entry_point_refuses_null_pointers_without_crashing():
+    """Each entry point that takes pointers, called with all of them NULL (sizes 1),
+    returns an error status (or 0 bytes) before it touches CUDA or dereferences an
+    argument -- in a child process, so a crash fails this test alone."""
+    import sys
+    res = subprocess.run([sys.executable, "-c", _NULL_PROBE], capture_output=True, text=True, cwd=ROOT, timeout=120)
+    assert res.returncode == 0, res.stderr[-2000:]
+    got = dict((ln.split()[0], int(ln.split()[1])) for ln in res.stdout.splitlines())
+    sizes = {n for n, (r, _) in _lib._SIGNATURES.items() if r is ctypes.c_size_t}
+    assert len(got) >= 20
+    for name, value in got.items():
+        if name in sizes:
+            assert value == 0, name
+        else:
+            assert value == _lib.GQA_ERR_NULL_POINTER, (name, value, _lib.status_string(value))
+
+
 def test_struct_layouts():
     assert ctypes.sizeof(_lib.GqaSeqDesc) == 24
     assert ctypes.sizeof(_lib.GqaParams) == 12 * 4 + 8 * 8 + 8 + 8
