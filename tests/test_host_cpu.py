@@ -10,6 +10,7 @@
 from __future__ import annotations
 
 import ctypes
+import os
 import hashlib
 import re
 import subprocess
@@ -106,6 +107,7 @@ def test_workspace_grows_without_freeing_the_old_buffer():
 
 _NULL_PROBE = r"""
 import ctypes
+import os
 from attention_accelerator_b200 import _lib
 lib = _lib.load()
 def is_ptr(a):
@@ -241,6 +243,13 @@ def test_plan_batch_descriptors_on_host():
     assert [d.kv_start for d in plan.host] == [0, 5, 14]
     assert [d.pos_end for d in plan.host] == [5, 9, 1]
     assert plan.device.numel() == 3 * 24
+
+
+def test_bench_parallel_read_mem_uses_every_core():
+    """The reference arm's .mem leg: read_mem on one spawned process per host core."""
+    import bench
+    value, cores, sample = bench.mem_cpu_run_parallel(0.2, lines_per_proc=512)
+    assert value > 0 and cores == (os.cpu_count() or 1) and f"{cores} pieces" in sample
 
 
 def test_bench_reference_arm_json_line():
