@@ -249,7 +249,7 @@ def test_bench_parallel_read_mem_uses_every_core():
     """The reference arm's .mem leg: read_mem on one spawned process per host core."""
     import bench
     value, cores, sample = bench.mem_cpu_run_parallel(0.2, lines_per_proc=512)
-    assert value > 0 and cores == (os.cpu_count() or 1) and f"{cores} pieces" in sample
+    assert value > 0 and cores == min(64, os.cpu_count() or 1) and f"{cores} pieces" in sample
 
 
 def test_bench_reference_arm_json_line():
