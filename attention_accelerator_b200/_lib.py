@@ -89,6 +89,8 @@ _SIGNATURES = {
     "gqa_decode_plan": (ctypes.c_int, [ctypes.POINTER(GqaParams), ctypes.POINTER(GqaSeqDesc), ctypes.c_int,
                                        ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int),
                                        ctypes.POINTER(ctypes.c_int)]),
+    "gqa_decode_plan_host": (ctypes.c_int, [ctypes.POINTER(GqaParams), ctypes.POINTER(GqaSeqDesc), ctypes.c_int,
+                                            ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "gqa_decode": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), _P, ctypes.c_size_t, _P]),
     "gqa_decode_noalloc": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), _P]),
     "gqa_decode_batched": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), ctypes.POINTER(GqaSeqDesc),

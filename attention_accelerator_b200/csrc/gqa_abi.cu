@@ -501,6 +501,34 @@ int gqa_decode_plan(const gqa_params* p, const gqa_seq_desc* descs, int batch, i
     return GQA_OK;
 }
 
+int gqa_decode_plan_host(const gqa_params* p, const gqa_seq_desc* descs, int batch, int sms, int* splits,
+                         int* keys_per_split) {
+    if (!p || !splits || !keys_per_split) return GQA_ERR_NULL_POINTER;
+    if (sms < 1) return GQA_ERR_BATCH;
+    int st = GQA_OK;
+    Plan pl;
+    // The planner asks the device only for cluster capacities; with clusters
+    // left out (clusters_ok = false) it makes no CUDA call.
+    if (descs == nullptr) {
+        if (batch != 1) return GQA_ERR_BATCH;
+        st = gqa_validate(p);
+        if (st != GQA_OK) return st;
+        const gqa::SeqDesc d = single_desc(p);
+        pl = make_plan(&d, 1, sms, true, false);
+    } else {
+        if (batch < 1) return GQA_ERR_BATCH;
+        const gqa::SeqDesc* d = reinterpret_cast<const gqa::SeqDesc*>(descs);
+        for (int b = 0; b < batch; ++b) {
+            st = check_desc(d[b], false);
+            if (st != GQA_OK) return st;
+        }
+        pl = make_plan(d, batch, sms, batch == 1, false);
+    }
+    *splits = pl.total_splits;
+    *keys_per_split = pl.chunk;
+    return GQA_OK;
+}
+
 int gqa_decode(const void* q, const void* k, const void* v, void* out, const gqa_params* p, void* workspace,
                size_t workspace_bytes, void* stream) {
     int st = gqa_validate(p);

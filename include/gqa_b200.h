@@ -178,6 +178,21 @@ int gqa_decode_plan(const gqa_params *p, const gqa_seq_desc *descs, int batch, i
                     int *cluster);
 
 /*
+ * Host-only planning (no reference counterpart): the split plan of a call on a
+ * GPU with `sms` SMs, computed without any CUDA call or device.  `descs`/`batch`
+ * as for gqa_workspace_bytes.  Thread-block clusters are left out, so the result
+ * equals gqa_decode_plan's on such a GPU whenever that reports cluster 0, as it
+ * does for every batch of several sequences and for long single sequences (on
+ * the B200s measured, for instance, SEQ_LEN 4096 and 131072).  For a scheduler
+ * that sizes work before it holds a GPU, and for tests of the planner on
+ * machines without one.  Writes the total
+ * number of key splits (each runs on 8 CTAs, one per KV head) and the keys per
+ * split.  Returns a status (GQA_ERR_BATCH for sms < 1).
+ */
+int gqa_decode_plan_host(const gqa_params *p, const gqa_seq_desc *descs, int batch, int sms, int *splits,
+                         int *keys_per_split);
+
+/*
  * Single-token decode of one sequence: the operation the reference performs
  * between START (axi_lite_regs.v:147-151) and the last output row
  * (gqa_attention_wrapper.v:186-222); numerically the golden of

@@ -137,6 +137,58 @@ def test_every_entry_point_refuses_null_pointers_without_crashing():
             assert value == _lib.GQA_ERR_NULL_POINTER, (name, value, _lib.status_string(value))
 
 
+def _host_plan(seq_len=None, seqs=None, sms=148):
+    sp, kp = ctypes.c_int(), ctypes.c_int()
+    lib = _lib.load()
+    if seqs is None:
+        p = make_params(seq_len=seq_len)
+        st = lib.gqa_decode_plan_host(ctypes.byref(p), None, 1, sms, ctypes.byref(sp), ctypes.byref(kp))
+    else:
+        p = make_params(seq_len=1)
+        arr = (_lib.GqaSeqDesc * len(seqs))()
+        start = 0
+        for i, n in enumerate(seqs):
+            arr[i].kv_start, arr[i].seq_len, arr[i].query_position = start, n, n - 1
+            arr[i].pos_begin, arr[i].pos_end = 0, n
+            start += n
+        st = lib.gqa_decode_plan_host(ctypes.byref(p), arr, len(seqs), sms, ctypes.byref(sp), ctypes.byref(kp))
+    assert st == _lib.GQA_OK, _lib.status_string(st)
+    return sp.value, kp.value
+
+
+def test_host_planner_reproduces_the_grids_measured_on_b200():
+    """The split planner, run without a GPU for 148 SMs, gives the grids ncu recorded
+    on the B200 (8 CTAs per split): config 2 136 CTAs, config 4 144, config 3 1088."""
+    assert _host_plan(4096) == (17, 248)       # one head group of SMs left for the next call
+    assert _host_plan(131072) == (18, 7288)
+    seqs = [int(x) for x in np.random.default_rng(20260805).integers(512, 8193, size=64)]  # bench config 3
+    assert sum(seqs) == 301934
+    assert _host_plan(seqs=seqs) == (136, 2800)
+    assert _host_plan(30) == (1, 88)
+
+
+@pytest.mark.parametrize("sms", [1, 8, 132, 148, 160])
+def test_host_planner_covers_every_key(sms):
+    rng = np.random.default_rng(sms)
+    for n in (1, 87, 88, 89, 4096, 65535, 131072):
+        splits, chunk = _host_plan(n, sms=sms)
+        assert chunk % 8 == 0 and 1 <= splits <= 64 and (splits - 1) * chunk < n <= splits * chunk
+    seqs = [int(x) for x in rng.integers(1, 20000, size=37)]
+    splits, chunk = _host_plan(seqs=seqs, sms=sms)
+    assert splits == sum(-(-n // chunk) for n in seqs)
+
+
+def test_host_planner_rejects_bad_arguments():
+    lib = _lib.load()
+    p = make_params(seq_len=100)
+    sp, kp = ctypes.c_int(), ctypes.c_int()
+    assert lib.gqa_decode_plan_host(ctypes.byref(p), None, 1, 0, ctypes.byref(sp), ctypes.byref(kp)) == _lib.GQA_ERR_BATCH
+    assert lib.gqa_decode_plan_host(ctypes.byref(p), None, 2, 148, ctypes.byref(sp), ctypes.byref(kp)) == _lib.GQA_ERR_BATCH
+    bad = make_params(seq_len=100, n_q_heads=31)
+    assert lib.gqa_decode_plan_host(ctypes.byref(bad), None, 1, 148, ctypes.byref(sp), ctypes.byref(kp)) == \
+        _lib.GQA_ERR_GEOMETRY
+
+
 def test_struct_layouts():
     assert ctypes.sizeof(_lib.GqaSeqDesc) == 24
     assert ctypes.sizeof(_lib.GqaParams) == 12 * 4 + 8 * 8 + 8 + 8
