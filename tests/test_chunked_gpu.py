@@ -162,3 +162,15 @@ def test_chunked_workspace_sizes(cuda_device):
     c1 = _lib.GqaChunkParams(batch=1, n_queries=37, first_position=100)
     p1 = make_params(seq_len=1000, query_position=136)
     assert lib.gqa_chunked_workspace_bytes(ctypes.byref(p1), ctypes.byref(c1)) == _lib.CHUNKED_WORKSPACE_BYTES
+
+
+def test_config5_full_batch(cuda_device):
+    """BASELINE config 5 at full size: 16 sequences, SEQ_LEN=8192, queries
+    8064..8191 -- 512 (sequence, Q head) units, 444 run whole and 68 split along
+    the keys and merged by the combine kernel.  Same bar as the other chunked
+    tests, with the FP32 bar on large outputs at 4 ULP instead of 2 for these
+    8.4 million outputs."""
+    b, n, s = 16, 128, 8192
+    q, k, v = chunk_inputs(b, n, s, seed=16)
+    got = run_chunked(q, k, v, cuda_device, s - n, s)
+    assert_chunk_parity(chunked_golden_f64(q, k, v, s, s - n), got, tight=4)
