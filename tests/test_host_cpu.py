@@ -189,6 +189,34 @@ def test_host_planner_rejects_bad_arguments():
         _lib.GQA_ERR_GEOMETRY
 
 
+def test_header_compiles_as_plain_c(tmp_path):
+    """include/gqa_b200.h is the boundary for C callers: a C99 translation unit that
+    includes it and takes the address of every declared function compiles without
+    warnings, and its struct sizes are the ones the Python binding uses."""
+    import shutil
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    names = declared_functions()
+    src = tmp_path / "abi.c"
+    src.write_text("#include \"gqa_b200.h\"\n#include <stdio.h>\n"
+                   "typedef void (*any_fn)(void);\n"
+                   "static const any_fn fns[] = {\n"
+                   + "".join(f"    (any_fn)&{n},\n" for n in names) + "};\n"
+                   "int main(void) {\n"
+                   "    printf(\"%zu %zu %zu %zu\\n\", sizeof(gqa_params), sizeof(gqa_seq_desc),\n"
+                   "           sizeof(gqa_partial_row), sizeof(fns) / sizeof(fns[0]));\n"
+                   "    return GQA_OK;\n}\n")
+    exe = tmp_path / "abi"
+    res = subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", str(ROOT / "include"),
+                          str(src), "-o", str(exe), "-Wl,--unresolved-symbols=ignore-all"],
+                         capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
+    assert [int(x) for x in out] == [ctypes.sizeof(_lib.GqaParams), ctypes.sizeof(_lib.GqaSeqDesc), 132 * 4,
+                                     len(names)]
+
+
 def test_struct_layouts():
     assert ctypes.sizeof(_lib.GqaSeqDesc) == 24
     assert ctypes.sizeof(_lib.GqaParams) == 12 * 4 + 8 * 8 + 8 + 8
