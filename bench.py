@@ -713,6 +713,24 @@ def chunked_cpu_run(budget_s: float, n_keys: int = 8192):
             return reps, dt
 
 
+def port_one_core(q, k, v, n, qpos, budget_s):
+    """The float64 restatement of the golden on one core (one worker, BLAS limited to
+    one thread): the single-core figure beside the all-cores one.  At least one call."""
+    from concurrent.futures import ThreadPoolExecutor
+    from threadpoolctl import threadpool_limits
+    from oracle.parallel import gqa_golden_parallel
+    with threadpool_limits(limits=1), ThreadPoolExecutor(max_workers=1) as pool:
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            gqa_golden_parallel(q, k, v, n, qpos, pool=pool)
+            reps += 1
+            dt = time.perf_counter() - t0
+            if dt >= budget_s or reps >= 200:
+                break
+    return {"value": round(kv_bytes(qpos + 1) * reps / dt / 1e9, 4), "cores": 1,
+            "sample": f"{reps} x SEQ_LEN={n} on one thread (BLAS limited to one), {dt:.1f} s"}
+
+
 def cpu_baseline(wl, budget_s=10.0):
     """Thread-parallel float64 restatement of the golden on this host (kind "port")."""
     import numpy as np
@@ -757,7 +775,8 @@ def cpu_baseline(wl, budget_s=10.0):
     out = {"value": round(kv_bytes(qpos + 1) * reps / dt / 1e9, 4), "unit": UNIT, "cores": threads,
            "kind": "port",
            "sample": f"{reps} x SEQ_LEN={s} decode(s) by the numpy float64 restatement (oracle/parallel.py), "
-                     f"{dt:.1f} s on {threads} threads"}
+                     f"{dt:.1f} s on {threads} threads",
+           "one_core": port_one_core(q, k, v, s, qpos, budget_s / 2)}
     if gpu is not None:
         res = check_rows(ref, gpu, 64)
         out["gpu_vs_port_ulp"] = {"max": res.worst_ulp, "mean": round(res.mean_ulp, 5), "pass_64": res.passed}
@@ -830,13 +849,15 @@ def reference_arm(args, rank, world):
     value = kv_bytes(n) * args.steps / dt / 1e9
     sample = (f"each step: the first {n} keys of the SEQ_LEN={s} workload (float64 numpy restatement of "
               f"gen_gqa_wrapper_vectors.py:121-139, {threads} threads)")
+    n1 = int(max(64, min(n, 10.0 / (per_key * threads))))  # about 10 s on one core
+    one = port_one_core(q, k[:, :n1], v[:, :n1], n1, n1 - 1, 10.0)
     print(json.dumps({
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic N(0,1) seeded",
         "impl": "reference", "config": {"workload": args.workload, "seq_len": s, "sample_keys": n},
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "one_core": one},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

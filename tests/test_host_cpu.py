@@ -344,4 +344,6 @@ def test_bench_reference_arm_json_line():
     assert line["impl"] == "reference" and line["unit"] == "GB/s" and line["value"] > 0
     assert line["metric"].startswith("decode-attn KV-read HBM GB/s")
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
+    one = line["cpu_baseline"]["one_core"]  # the single-core figure beside the all-cores one
+    assert one["cores"] == 1 and one["value"] > 0
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
