@@ -332,6 +332,20 @@ def test_bench_parallel_read_mem_uses_every_core():
     assert value > 0 and cores == min(64, os.cpu_count() or 1) and f"{cores} pieces" in sample
 
 
+def test_bench_cpu_baseline_reports_all_cores_and_one_core():
+    """Our arm's cpu_baseline for a workload without oracle inputs (configs 3 and 4):
+    the float64 port on a config-2-sized sample, on all cores and on one."""
+    import bench
+
+    class Sampled:
+        def oracle_inputs(self):
+            return None
+
+    out = bench.cpu_baseline(Sampled(), budget_s=0.3)
+    assert out["kind"] == "port" and out["value"] > 0 and out["cores"] == (os.cpu_count() or 1)
+    assert out["one_core"]["cores"] == 1 and out["one_core"]["value"] > 0
+
+
 def test_bench_reference_arm_json_line():
     """`bench.py --impl reference` (the reference algorithm on the host cores) prints one
     JSON line with the contract's keys; config 1 keeps it to a few seconds."""
