@@ -50,6 +50,19 @@ def test_fast_oracle_agrees_with_exact(manifest):
         assert check_rows(golden, fast, 0).worst_ulp <= 1
 
 
+def test_parallel_port_agrees_with_the_pinned_golden(manifest):
+    """The thread-parallel float64 port that bench.py times as the reference's CPU
+    path (oracle/parallel.py) gives the reference golden files within 1 ULP,
+    including a causal case and slab boundaries (1024 keys per slab)."""
+    from oracle.parallel import gqa_golden_parallel
+    for name in ("random_len30", "causal_len100_q63", "random_len1024", "random_len256"):
+        case = generate_case(**case_kwargs(manifest["cases"][name]["args"]))
+        golden = read_mem_array(GOLDEN / "cases" / name / "gqa_golden.mem", 128)
+        got = gqa_golden_parallel(case.q_bits, case.k_bits, case.v_bits, case.seq_len, case.query_position,
+                                  threads=4, slab=96)
+        assert check_rows(golden, got, 0).worst_ulp <= 1, name
+
+
 def test_corpus_65536_is_the_len30_case(manifest):
     """README.md:121-138: 65,536 valid elements select SEQ_LEN=30 with two pad rows."""
     c = manifest["cases"]
