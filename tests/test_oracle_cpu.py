@@ -63,6 +63,24 @@ def test_parallel_port_agrees_with_the_pinned_golden(manifest):
         assert check_rows(golden, got, 0).worst_ulp <= 1, name
 
 
+@pytest.mark.parametrize("seq_len,first,n", [(300, 280, 20), (300, 100, 16), (64, 0, 64)])
+def test_chunked_oracle_is_the_per_query_golden(seq_len, first, n):
+    """oracle/chunked.py (the checker of the tensor-core path and config 5's CPU
+    baseline) answers query i exactly as the single-position golden with
+    QUERY_POSITION = first + i (gen_gqa_wrapper_vectors.py:121-139)."""
+    from oracle import chunked_golden_f64
+    from oracle.golden import gqa_golden_f64
+    rng = np.random.default_rng(seq_len + first)
+    q = f32_to_bf16(rng.standard_normal((2, n, 32, 128)).astype(np.float32))
+    k = f32_to_bf16(rng.standard_normal((2, 8, seq_len, 128)).astype(np.float32))
+    v = f32_to_bf16(rng.standard_normal((2, 8, seq_len, 128)).astype(np.float32))
+    got = chunked_golden_f64(q, k, v, seq_len, first)
+    for b in range(2):
+        for i in range(0, n, 3):
+            want = gqa_golden_f64(q[b, i], k[b], v[b], seq_len, first + i, exact=False)
+            np.testing.assert_allclose(got[b, i], want, rtol=1e-12, atol=1e-15)
+
+
 def test_corpus_65536_is_the_len30_case(manifest):
     """README.md:121-138: 65,536 valid elements select SEQ_LEN=30 with two pad rows."""
     c = manifest["cases"]
