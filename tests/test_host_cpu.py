@@ -346,6 +346,14 @@ def test_bench_cpu_baseline_reports_all_cores_and_one_core():
     assert out["one_core"]["cores"] == 1 and out["one_core"]["value"] > 0
 
 
+def test_bench_chunked_cpu_run_is_bounded():
+    """config 5's CPU leg: whole sequences of the float64 chunked restatement, at
+    least one, stopping at the budget."""
+    import bench
+    reps, dt = bench.chunked_cpu_run(0.05, n_keys=256)
+    assert reps >= 1 and dt > 0
+
+
 def test_bench_reference_arm_json_line():
     """`bench.py --impl reference` (the reference algorithm on the host cores) prints one
     JSON line with the contract's keys; config 1 keeps it to a few seconds."""
