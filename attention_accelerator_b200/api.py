@@ -8,10 +8,12 @@ register programming raises :class:`GqaConfigError` before anything is
 launched, as the RTL's ``config_error`` rejects a START
 (gqa_attention_wrapper.v:230-237).
 
-Tensors are torch tensors.  CUDA inputs are used in place; CPU inputs are
-copied to the current CUDA device and the result is copied back (the
-end-to-end path).  Every operation runs in ``lib/libgqa_b200.so``; there is no
-CPU implementation.
+Tensors are torch tensors.  CUDA inputs are used in place; ``decode`` also
+takes CPU inputs, copies them to the current CUDA device and copies the result
+back (the end-to-end path), while the other entry points refuse CPU tensors.
+Tensors of one call must share a device, and a caller's ``out`` must hold every
+row the kernel writes; both are checked before anything is launched.  Every
+operation runs in ``lib/libgqa_b200.so``; there is no CPU implementation.
 """
 from __future__ import annotations
 
