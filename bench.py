@@ -3,13 +3,16 @@
 KV-read HBM GB/s, % of the measured HBM peak, and query-heads/s, at 1/2/4/8 B200).
 
 One step = one pass of the hot path over one batch of synthetic input:
-  config2 (default): one single-token decode, SEQ_LEN=4096, QUERY_POSITION=4095,
-                     position-major BF16 KV cache [4096, 8, 128] per GPU.
+  config4 (default): one single-token decode, SEQ_LEN=131072, QUERY_POSITION=131071,
+                     position-major BF16 KV cache [131072, 8, 128] -- the largest
+                     single-sequence BASELINE configuration; at N>1 GPUs the
+                     sequence is split into contiguous shards whose (m, l, O) rows
+                     are exchanged over NVLink peer memory inside the decode kernel
+                     and merged by log-sum-exp (strong scaling; --exchange nccl: an
+                     NCCL all-gather + combine kernel instead).
+  config2:           SEQ_LEN=4096, QUERY_POSITION=4095 (one sequence per GPU).
   config1:           SEQ_LEN=30, QUERY_POSITION=29, KV_BLOCK_LEN=16, U[-1,1) inputs.
   config3:           batch 64, SEQ_LEN ~ U{512..8192}, K with log-normal channel scales.
-  config4:           SEQ_LEN=131072; at N>1 GPUs the sequence is split into
-                     contiguous shards, FP32 partials are all-gathered over NCCL and
-                     merged by the LSE combine kernel (strong scaling).
   config5:           chunked multi-query decode on the tensor cores: batch 16,
                      SEQ_LEN=8192, queries 8064..8191 per sequence (causal); the 16
                      sequences are split across ranks (strong scaling).  Its roofline
@@ -20,7 +23,10 @@ collective (weak scaling).
 Timing: K steps replayed from CUDA graphs on one stream between CUDA events,
 after W warm-up steps, barrier + synchronize on both sides, max over ranks.
 Inputs rotate over buffer sets whose total exceeds twice the L2 size, so every
-step reads K/V from HBM.  ``--impl reference`` times the CPU restatement of the
+step reads K/V from HBM.  After timing, every rank checks the output of the last
+timed step against an independent decode of the same inputs (``check`` in the
+JSON line): another split plan and merge on the same GPU, and for the sequence
+split a single-GPU decode of the whole sequence.  ``--impl reference`` times the CPU restatement of the
 reference golden (the reference itself is Python that cannot run on the GPU box)
 on all host threads.
 """
@@ -53,6 +59,32 @@ def kv_bytes(n_keys: int) -> int:
     return 2 * n_keys * 8 * 128 * 2 + 2 * HEAD_BYTES
 
 
+def _ordered(codes):
+    """BF16 codes as integers that order like the values (sign-magnitude to two's complement)."""
+    import numpy as np
+    c = np.asarray(codes).astype(np.int64) & 0xFFFF
+    return np.where(c & 0x8000, 0x8000 - c, c)
+
+
+def compare_outputs(got, want, what: str) -> dict:
+    """BF16 outputs of the timed steps (`got`) against an independent decode of the
+    same inputs (`want`), rows of 128: per-element code distance, the count beyond
+    the reference's 64-ULP limit, and the worst distance where the output is at
+    least 2^-10 of its row's largest magnitude.  ok: none beyond 64, <= 2 on those."""
+    import numpy as np
+    import torch
+    g = got.detach().reshape(-1, 128).contiguous().view(torch.int16).cpu().numpy()
+    w = want.detach().reshape(-1, 128).contiguous().view(torch.int16).cpu().numpy()
+    dist = np.abs(_ordered(g) - _ordered(w))
+    mag = np.abs(want.detach().reshape(-1, 128).float().cpu().numpy())
+    big = mag >= np.ldexp(mag.max(axis=1, keepdims=True), -10)
+    beyond = int((dist > 64).sum())
+    large = int(dist[big].max(initial=0))
+    return {"ok": beyond == 0 and large <= 2 and bool(np.isfinite(mag).all()), "against": what,
+            "outputs": int(dist.size), "max_ulp": int(dist.max(initial=0)), "max_ulp_large_outputs": large,
+            "beyond_64_ulp": beyond, "mean_ulp": round(float(dist.mean()), 5)}
+
+
 def peak_bf16():
     """Dense BF16 tensor peak: the measured burst figure (a kernel timed alone)."""
     path = ROOT / "MEASURED_PEAKS.json"
@@ -75,7 +107,7 @@ class ClockSampler:
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,clocks.mem")
 
     def __init__(self, gpu_index: int):
         self.rows, self.window = [], None
@@ -115,8 +147,9 @@ class ClockSampler:
         smax = [float(r[2]) for r in rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows if len(r) > 8 for n, v in zip(names, r[5:9]) if v == "Active"})
+        mem = [float(r[9]) for r in rows if len(r) > 9 and r[9].replace(".", "").isdigit()]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(rows)}
+                "mem_mhz": statistics.median(mem) if mem else None, "reasons": reasons, "samples": len(rows)}
 
 
 # ---------------------------------------------------------------------------
@@ -140,6 +173,24 @@ class Workload:
     @property
     def sets(self) -> int:
         return 1
+
+
+def split_reference(gqa, torch, q, k, v, seq_len, qpos, layout="position_major", k_rotated=False, shards=2):
+    """One sequence decoded as `shards` contiguous key ranges (FP32 partial rows
+    of decode_batch) merged by combine_partials: a different split plan and
+    merge from a single decode call, for checking its output."""
+    dev = q.device
+    n = qpos + 1
+    bounds = [round(i * n / shards) for i in range(shards + 1)]
+    parts = []
+    for lo, hi in zip(bounds[:-1], bounds[1:]):
+        plan = gqa.plan_batch([seq_len], query_positions=[qpos], pos_begin=[lo], pos_end=[hi], kv_starts=[0],
+                              partial=True, device=dev)
+        kk = k[lo:hi] if layout == "position_major" else k[:, lo:hi].transpose(0, 1)
+        vv = v[lo:hi] if layout == "position_major" else v[:, lo:hi].transpose(0, 1)
+        parts.append(gqa.decode_batch(q.reshape(1, 32, 128), kk.contiguous(), vv.contiguous(), plan,
+                                      k_rotated=k_rotated))
+    return gqa.combine_partials(torch.stack(parts))[0]
 
 
 class SingleDecode(Workload):
@@ -189,6 +240,14 @@ class SingleDecode(Workload):
         return {"workload": self.name, "batch_per_gpu": 1, "seq_len": self.S, "query_position": self.qpos,
                 "kv_block_len": 16, "kv_layout": f"{lay} bf16", "l2": self.l2_note,
                 "splits": f"{sp.splits} x {sp.keys_per_split} keys x 8 KV heads ({merge})"}
+
+    def check(self, steps: int) -> dict:
+        """The last timed step's output against the same inputs decoded as two
+        key shards (FP32 partials of decode_batch) merged by combine_partials."""
+        j = (steps - 1) % self.nsets
+        return compare_outputs(self.out, split_reference(self.gqa, self.torch, self.q[j], self.k[j], self.v[j],
+                                                         self.S, self.qpos, self.layout, self.k_rotated),
+                               "2 key shards (decode_batch partials) + combine_partials, same inputs")
 
     def e2e_inputs(self):
         t = self.torch
@@ -265,6 +324,17 @@ class RaggedBatch(Workload):
                 "total_keys": sum(self.seq), "kv_layout": "packed position_major [sum S,8,128] bf16",
                 "k_channel_scale": "exp(N(0,1)) per (kv head, dim)", "l2": self.l2_note}
 
+    def check(self, steps: int) -> dict:
+        """The last timed step's 64 outputs against each sequence decoded on its own
+        (gqa.decode: a single-sequence split plan and the in-kernel merge)."""
+        j = (steps - 1) % self.nsets
+        want, start = [], 0
+        for b, n in enumerate(self.seq):
+            want.append(self.gqa.decode(self.q[j][b], self.k[j][start:start + n], self.v[j][start:start + n],
+                                        seq_len=n, k_rotated=self.k_rotated))
+            start += n
+        return compare_outputs(self.out, self.torch.stack(want), "each sequence decoded alone (gqa.decode)")
+
     def e2e_inputs(self):
         return [x.cpu().pin_memory() for x in (self.q[0], self.k[0], self.v[0])]
 
@@ -301,12 +371,17 @@ class LongContext(Workload):
         self.lo, self.hi = lo, hi
         per_set = 2 * (hi - lo) * 8 * 128 * 2
         self.nsets = max(2, math.ceil(2 * L2_BYTES / per_set))
-        g = torch.Generator(device=device).manual_seed(seed)  # same Q on all ranks
-        self.q = [torch.randn((1, 32, 128), generator=g, device=device).to(torch.bfloat16) for _ in range(self.nsets)]
-        self.k = [torch.randn((hi - lo, 8, 128), generator=g, device=device).to(torch.bfloat16)
-                  for _ in range(self.nsets)]
-        self.v = [torch.randn((hi - lo, 8, 128), generator=g, device=device).to(torch.bfloat16)
-                  for _ in range(self.nsets)]
+        # Every rank generates the same whole sequences (same seed) and decodes
+        # its contiguous shard of them (a view); the whole sequence is kept for
+        # the output check, a single-GPU decode of it.
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.q, self.kfull, self.vfull = [], [], []
+        for _ in range(self.nsets):
+            self.q.append(torch.randn((1, 32, 128), generator=g, device=device).to(torch.bfloat16))
+            self.kfull.append(torch.randn((seq_len, 8, 128), generator=g, device=device).to(torch.bfloat16))
+            self.vfull.append(torch.randn((seq_len, 8, 128), generator=g, device=device).to(torch.bfloat16))
+        self.k = [x[lo:hi] for x in self.kfull]
+        self.v = [x[lo:hi] for x in self.vfull]
         self.device = device
         if world == 1:
             self.out = torch.empty((32, 128), dtype=torch.bfloat16, device=device)
@@ -360,6 +435,48 @@ class LongContext(Workload):
                 "parallelism": f"sequence split x{self.world}, {xchg}" if self.world > 1 else "single GPU",
                 "l2": self.l2_note}
 
+    def check(self, steps: int) -> dict:
+        """The last timed step's output (every rank's, at N > 1) against a
+        single-GPU decode of the whole sequence (at N = 1: four key shards
+        merged by combine_partials)."""
+        j = (steps - 1) % self.nsets
+        if self.world == 1:
+            want = split_reference(self.gqa, self.torch, self.q[j][0], self.kfull[j], self.vfull[j], self.S,
+                                   self.S - 1, k_rotated=self.k_rotated, shards=4)
+            what = "4 key shards (decode_batch partials) + combine_partials, same inputs"
+        else:
+            want = self.gqa.decode(self.q[j][0], self.kfull[j], self.vfull[j], seq_len=self.S,
+                                   k_rotated=self.k_rotated)
+            what = "single-GPU decode of the whole sequence on this rank"
+        return compare_outputs(self.out, want, what)
+
+    def breakdown(self, torch, steps, warmup, stream, dist_on) -> dict | None:
+        """At N > 1: the shard decode alone (FP32 partial rows, no exchange), timed
+        as the step is; the rest of the step is the exchange and the merge."""
+        if self.world == 1:
+            return None
+        gqa = self.gqa
+        plan = gqa.plan_batch([self.S], pos_begin=[self.lo], pos_end=[self.hi], kv_starts=[0], partial=True,
+                              device=self.device)
+        part = torch.empty((1, 32, 132), dtype=torch.float32, device=self.device)
+        outer = self
+
+        class ShardOnly(Workload):
+            graph_ok = True
+
+            @property
+            def sets(self):
+                return outer.nsets
+
+            def launch(self, i):
+                j = i % outer.nsets
+                gqa.decode_batch(outer.q[j], outer.k[j], outer.v[j], plan, out=part, k_rotated=outer.k_rotated)
+
+        ms, _ = timed_graph_run(torch, ShardOnly(), steps, warmup, stream, dist_on)
+        t = torch.tensor([ms], dtype=torch.float64, device=self.device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return {"shard_decode_us": round(float(t.item()) / steps * 1e3, 3)}
+
     def e2e_inputs(self):
         return [x.cpu().pin_memory() for x in (self.q[0], self.k[0], self.v[0])]
 
@@ -384,10 +501,22 @@ class LongContext(Workload):
             self.peer.close()
 
     def oracle_inputs(self):
-        return None
+        """Head-major BF16 codes of buffer set 0 (the whole sequence) for the CPU port."""
+        import numpy as np
+        t = self.torch
+
+        def bits(x):
+            return x.contiguous().view(t.int16).cpu().numpy().astype(np.uint16)
+        return (bits(self.q[0][0]), bits(self.kfull[0].transpose(0, 1)), bits(self.vfull[0].transpose(0, 1)),
+                self.S, self.S - 1)
 
     def gpu_result_set0(self):
-        return None
+        import numpy as np
+        if self.k_rotated or self.world > 1:
+            return None
+        self.launch(0)
+        self.torch.cuda.synchronize()
+        return self.out.view(self.torch.int16).cpu().numpy().astype(np.uint16)
 
 
 class ChunkedDecode(Workload):
@@ -450,6 +579,20 @@ class ChunkedDecode(Workload):
                 "precision": "Q, K, P each split into three BF16 parts: 6 Q.K + 3 P.V tensor-core products "
                              "(FP32-equivalent); executed tensor FLOPs = 4.5 x algorithmic"}
 
+    def check(self, steps: int) -> dict:
+        """Queries 0, 63 and 127 of every local sequence of the last timed step
+        against single-position calls of the decode kernel (gqa.decode at that
+        QUERY_POSITION): another kernel, and the BASELINE's stated equivalence."""
+        j = (steps - 1) % self.nsets
+        got, want = [], []
+        for b in range(self.local):
+            for i in (0, self.n // 2 - 1, self.n - 1):
+                got.append(self.out[b, i])
+                want.append(self.gqa.decode(self.q[j][b, i], self.k[j][b], self.v[j][b], seq_len=self.S,
+                                            query_position=self.first + i))
+        return compare_outputs(self.torch.stack(got), self.torch.stack(want),
+                               "queries 0, 63, 127 of each sequence by single-position gqa.decode calls")
+
     def e2e_inputs(self):
         return [x.cpu().pin_memory() for x in (self.q[0], self.k[0], self.v[0])]
 
@@ -511,9 +654,10 @@ class MemCodec(Workload):
                                      self.torch.cuda.current_stream().cuda_stream)
         assert st == 0, st
 
-    def check(self):
+    def check(self, steps: int) -> dict:
         n, bad = (int(x) for x in self.result.cpu())
-        assert bad == -1 and n == self.n_rows and self.torch.equal(self.rows, self.want), "memcodec decode mismatch"
+        ok = bad == -1 and n == self.n_rows and bool(self.torch.equal(self.rows, self.want))
+        return {"ok": ok, "against": "the codes the text was encoded from (byte-exact)", "rows": n}
 
     def config(self):
         return {"workload": self.name, "file": "gqa_k.mem of config 4 (head-major [8][131072][128], 16 codes a line)",
@@ -671,6 +815,20 @@ def traffic_for(workload: str, bytes_per_launch: float):
     if abs(alg - bytes_per_launch) > 1e-3 * bytes_per_launch:
         return None
     return rec.get("dram_bytes_per_launch")
+
+
+def pinned_h2d_gbs(torch, nbytes: int, device, reps: int = 20) -> float:
+    """Plain host-to-device copy rate of one pinned buffer of `nbytes` on this box
+    (wall clock around synchronised copies, as e2e is timed): what e2e is bound by."""
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    dev.copy_(host, non_blocking=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        dev.copy_(host, non_blocking=True)
+    torch.cuda.synchronize()
+    return nbytes * reps / (time.perf_counter() - t0) / 1e9
 
 
 def e2e_run(torch, wl, steps, device):
@@ -869,7 +1027,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=("config1", "config2", "config3", "config4", "config5", "memcodec"),
-                    default="config2")
+                    default="config4")
     ap.add_argument("--layout", choices=("position_major", "head_major"), default="position_major")
     ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
@@ -923,14 +1081,26 @@ def main():
     per_gpu_bytes = wl.bytes_per_step if wl.scaling == "weak" else wl.bytes_per_step / world
     achieved = per_gpu_bytes / (ms_step * 1e-3) / 1e9
 
-    if hasattr(wl, "check"):
-        wl.check()  # the timed steps' output is the expected decode
-    e2e_dt, h2d, d2h = e2e_run(torch, wl, args.e2e_steps, device)
+    check = wl.check(args.steps) if hasattr(wl, "check") else None  # the last timed step's output
+    if check is not None and not check["ok"]:
+        print(f"bench: output check FAILED on rank {rank}: {check}", file=sys.stderr, flush=True)
     if dist_on:
-        t = torch.tensor([e2e_dt], dtype=torch.float64, device=device)
+        t = torch.tensor([1.0 if check is None or check["ok"] else 0.0], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+        if check is not None:
+            check["all_ranks_ok"] = bool(t.item() == 1.0)
+    breakdown = wl.breakdown(torch, args.steps, args.warmup, stream, dist_on) if hasattr(wl, "breakdown") else None
+    if breakdown:
+        breakdown["step_us"] = round(ms_step * 1e3, 3)
+        breakdown["exchange_and_merge_us"] = round(breakdown["step_us"] - breakdown["shard_decode_us"], 3)
+    e2e_dt, h2d, d2h = e2e_run(torch, wl, args.e2e_steps, device)
+    copy_gbs = pinned_h2d_gbs(torch, h2d, device)
+    if dist_on:
+        t = torch.tensor([e2e_dt, -copy_gbs], dtype=torch.float64, device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_dt = float(t.item())
+        e2e_dt, copy_gbs = float(t[0].item()), -float(t[1].item())  # slowest rank's e2e and copy
     e2e_value = wl.bytes_per_step * scale * args.e2e_steps / e2e_dt / 1e9
+    e2e_h2d_gbs = h2d * args.e2e_steps / e2e_dt / 1e9  # this rank's host bytes per second of e2e
     clocks = sampler.stop() if sampler else None
 
     cpu = None
@@ -967,7 +1137,11 @@ def main():
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 3), "unit": getattr(wl, "unit", UNIT), "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": args.e2e_steps},
+                    "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
+                    "pinned_h2d_copy_gbs": round(copy_gbs, 2),
+                    "h2d_rate_of_pinned_copy": round(e2e_h2d_gbs / copy_gbs, 4)},
+            "check": check,
+            "breakdown": breakdown,
             "gpu_launches": args.steps * wl.launches_per_step,
             "clocks": clocks,
         }

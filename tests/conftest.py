@@ -74,35 +74,60 @@ def cuda_device():
     return torch.device("cuda", 0)
 
 
-CANCEL_FLOOR = 2.0 ** -18   # below this fraction of the row max the 64-ULP rule is not FP32-attainable
-ABS_BOUND = 2.0 ** -20      # absolute bound there, as a fraction of the row max
+RESIDUE_FLOOR = 2.0 ** -18  # |golden| below this fraction of its row's largest: a cancellation residue
+RESIDUE_ERR = 2.0 ** -20    # absolute error allowed on an accepted exception, as a fraction of the row max
 
 
-def assert_chunk_parity(golden64, got, tight: int = 2):
-    """Parity against a float64 golden where outputs may cancel to a few FP32
-    ulps of their row: the reference's 64-ULP rule (pyfiles/check_gqa_output.py:
-    55-75) on every element at least CANCEL_FLOOR of its row's largest magnitude,
-    an absolute error of at most ABS_BOUND of the row's largest below that (FP32
-    arithmetic itself cannot hold 64 ULP there: a float32 restatement of the
-    golden misses the strict rule on about 1 element in 262,144), and this
-    build's FP32 bar on the rest (<= `tight` ULP where the golden is at least
-    2^-10 of its row's largest, mean ULP < 0.1 over the strict elements).
-    Returns the count of
-    strict-rule exceptions."""
-    from oracle import check_rows
+def parity_exceptions(golden64, got):
+    """Elements that fail the reference's rule exactly as pyfiles/check_gqa_output.py:
+    57-69 applies it: BF16-code distance above 64 unless BOTH exponent fields are
+    <= 0x3d.  Returns (exceptions, ulp distance, golden BF16 codes, row max), each
+    exception a dict with its position, golden and output values, ULP and the
+    magnitudes relative to its row's largest output."""
     from oracle.bf16 import bf16_to_f32, f32_to_bf16, ulp_distance
-    golden = f32_to_bf16(np.asarray(golden64)).reshape(-1, 128)
     g64 = np.asarray(golden64, dtype=np.float64).reshape(-1, 128)
+    golden = f32_to_bf16(g64)
     got = np.asarray(got).reshape(-1, 128)
-    res = check_rows(golden, got, 64)
     dist = ulp_distance(golden, got)
+    exempt = ((((golden.astype(np.int64) >> 7) & 0xFF) <= 0x3D) &
+              (((got.astype(np.int64) >> 7) & 0xFF) <= 0x3D))
     rowmax = np.abs(g64).max(axis=-1, keepdims=True)
-    strict = np.abs(g64) >= CANCEL_FLOOR * rowmax
-    exempt = ((golden.astype(np.int64) >> 7) & 0xFF) <= 0x3D
-    assert not np.any((dist > 64) & strict & ~exempt), res.line()
-    err = np.abs(bf16_to_f32(got).astype(np.float64) - g64)
-    assert np.all(strict | (err <= ABS_BOUND * rowmax)), float((err / rowmax)[~strict].max())
+    out = []
+    for r, c in zip(*np.nonzero((dist > 64) & ~exempt)):
+        a = float(bf16_to_f32(got[r, c]))
+        out.append({"row": int(r), "col": int(c), "golden": float(g64[r, c]), "got": a, "ulp": int(dist[r, c]),
+                    "golden_of_rowmax": float(abs(g64[r, c]) / rowmax[r, 0]),
+                    "err_of_rowmax": float(abs(a - g64[r, c]) / rowmax[r, 0])})
+    return out, dist, golden, rowmax
+
+
+def assert_chunk_parity(golden64, got, tight: int = 2, max_exceptions: int = 0, label: str = ""):
+    """Parity against a float64 golden, held to the reference's per-element rule.
+
+    * The reference's rule (pyfiles/check_gqa_output.py:55-75: <= 64 BF16 ULP
+      unless both exponents are <= 0x3d) on every element.  At most
+      `max_exceptions` elements may miss it, and only as bounded cancellation
+      residues: golden below RESIDUE_FLOOR of its row's largest magnitude and
+      absolute error at most RESIDUE_ERR of it.  The rule has no relative
+      floor, so an output that cancels to ~2^-22 of its row is as strict as
+      FP32 arithmetic itself; each caller that allows exceptions states the
+      measured count.
+    * This build's FP32 bar: <= `tight` ULP wherever the golden is at least
+      2^-10 of its row's largest magnitude, mean ULP < 0.1 over the elements
+      at least RESIDUE_FLOOR of it.
+    Prints the exception count, worst and mean ULP (and each exception), and
+    returns the exception list."""
+    exc, dist, golden, rowmax = parity_exceptions(golden64, got)
+    g64 = np.asarray(golden64, dtype=np.float64).reshape(-1, 128)
+    print(f"parity {label}: {dist.size} outputs, {len(exc)} beyond 64 ULP (reference rule), "
+          f"worst {int(dist.max(initial=0))} ULP, mean {float(dist.mean()):.5f} ULP")
+    for e in exc:
+        print(f"  exception {e}")
+    assert len(exc) <= max_exceptions, exc
+    for e in exc:
+        assert e["golden_of_rowmax"] < RESIDUE_FLOOR and e["err_of_rowmax"] <= RESIDUE_ERR, e
     big = np.abs(g64) >= np.ldexp(rowmax, -10)
-    assert int(dist[big].max(initial=0)) <= tight, res.line()
-    assert dist[strict].mean() < 0.1, res.line()  # the mean where the ULP metric means something
-    return int(np.sum((dist > 64) & ~exempt))
+    assert int(dist[big].max(initial=0)) <= tight, f"worst {int(dist[big].max())} ULP on large outputs"
+    strict = np.abs(g64) >= RESIDUE_FLOOR * rowmax
+    assert dist[strict].mean() < 0.1, float(dist[strict].mean())
+    return exc

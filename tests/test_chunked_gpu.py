@@ -5,13 +5,12 @@ position ("equivalent to 128 sequential single-position
 reference calls per sequence").
 
 Bound (``assert_chunk_parity``):
-  * the reference's 64-ULP rule (pyfiles/check_gqa_output.py:55-75) on every
-    element whose golden magnitude is at least 2^-18 of its row's largest;
-  * below that (outputs that cancel to a few FP32 ulps of the row), an absolute
-    error of at most 2^-20 of the row's largest magnitude.  FP32 arithmetic
-    itself cannot hold 64 ULP there: a float32 restatement of the golden
-    misses the strict rule on about 1 element in 262,144 at S=2048, and the
-    CUDA-core decode kernel reaches 50 ULP on the same elements;
+  * the reference's 64-ULP rule (pyfiles/check_gqa_output.py:55-75, exemption
+    only when both exponents are <= 0x3d) on every element; the full-size
+    config-5 test allows its measured, listed exceptions: cancellation
+    residues (golden < 2^-18 of its row's largest magnitude, error <= 2^-20 of
+    it), which the rule, having no relative floor, makes as strict as FP32
+    arithmetic itself;
   * this build's FP32 bar on the rest: <= 2 ULP where the golden is at least
     2^-10 of its row's largest magnitude, mean ULP < 0.1.
 """
@@ -164,13 +163,21 @@ def test_chunked_workspace_sizes(cuda_device):
     assert lib.gqa_chunked_workspace_bytes(ctypes.byref(p1), ctypes.byref(c1)) == _lib.CHUNKED_WORKSPACE_BYTES
 
 
+# Config 5's measured exceptions to the reference's rule (B200, this seed): 3 of
+# the 8,388,608 outputs, each a cancellation residue -- golden 0.16-0.77 x 10^-6
+# of its row's largest magnitude, absolute error 0.07-0.33 x 10^-6 of it (109,
+# 323 and 111 BF16 ULP).  Every other output is within 64 ULP, worst 1 ULP on
+# outputs above 2^-10 of their row.
+CONFIG5_EXCEPTIONS = 3
+
+
 def test_config5_full_batch(cuda_device):
     """BASELINE config 5 at full size: 16 sequences, SEQ_LEN=8192, queries
     8064..8191 -- 512 (sequence, Q head) units, 444 run whole and 68 split along
-    the keys and merged by the combine kernel.  Same bar as the other chunked
-    tests, with the FP32 bar on large outputs at 4 ULP instead of 2 for these
-    8.4 million outputs."""
+    the keys and merged by the combine kernel.  The reference's rule on all
+    8.4 million outputs, with the counted, bounded exception list above."""
     b, n, s = 16, 128, 8192
     q, k, v = chunk_inputs(b, n, s, seed=16)
     got = run_chunked(q, k, v, cuda_device, s - n, s)
-    assert_chunk_parity(chunked_golden_f64(q, k, v, s, s - n), got, tight=4)
+    assert_chunk_parity(chunked_golden_f64(q, k, v, s, s - n), got, max_exceptions=CONFIG5_EXCEPTIONS,
+                        label="config 5 (16 x 128 queries)")

@@ -335,9 +335,9 @@ def test_config3_full_batch(cuda_device):
     """BASELINE config 3 at full size: the bench's 64 sequence lengths
     (U{512..8192}, 301,934 keys, K with per-channel outlier scales) in one
     launch of 1088 CTAs plus the split merge, each sequence against the float64
-    oracle.  Bar: the reference's 64-ULP rule with the cancellation floor
-    (``assert_chunk_parity``); the FP32 bar on large outputs is 4 ULP instead
-    of 2 for these 262,144 outputs."""
+    oracle.  Bar: the reference's per-element rule on all 262,144 outputs with
+    no exception (``assert_chunk_parity``, measured on B200: 0 beyond 64 ULP,
+    worst 43 ULP on a near-zero output), <= 2 ULP on large outputs."""
     from conftest import assert_chunk_parity
     from oracle.golden import gqa_golden_f64
     seqs = [int(x) for x in np.random.default_rng(20260805).integers(512, 8193, size=64)]
@@ -350,6 +350,7 @@ def test_config3_full_batch(cuda_device):
     out = gqa.decode_batch(bits_to_torch(qs, cuda_device), bits_to_torch(k, cuda_device),
                            bits_to_torch(v, cuda_device), plan)
     got = torch_to_bits(out)
-    for i, s in enumerate(seqs):
-        golden = gqa_golden_f64(parts[i][0], parts[i][1], parts[i][2], s, s - 1, exact=False)
-        assert_chunk_parity(golden, got[i], tight=4)
+    golden = np.stack([gqa_golden_f64(parts[i][0], parts[i][1], parts[i][2], s, s - 1, exact=False)
+                       for i, s in enumerate(seqs)])
+    assert_chunk_parity(golden, got, max_exceptions=0, label="config 3 (64 ragged sequences)")
+

@@ -369,3 +369,26 @@ def test_bench_reference_arm_json_line():
     one = line["cpu_baseline"]["one_core"]  # the single-core figure beside the all-cores one
     assert one["cores"] == 1 and one["value"] > 0
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_bench_output_check_counts_ulps_like_the_reference():
+    """bench.compare_outputs: BF16 code distance across zero, the 64-ULP count and
+    the bar on large outputs (<= 2 ULP where |x| >= 2^-10 of the row's largest)."""
+    import torch
+    import bench
+    want = torch.zeros((2, 128), dtype=torch.bfloat16)
+    want[0, :] = 1.0
+    want[1, 0] = 4.0
+    want[1, 1] = 2.0 ** -20                      # tiny next to 4.0: not a large output
+    got = want.clone()
+    res = bench.compare_outputs(got, want, "same")
+    assert res["ok"] and res["max_ulp"] == 0 and res["beyond_64_ulp"] == 0
+    got[0, 5] = torch.tensor(1.0).to(torch.bfloat16).view(torch.int16).add(2).view(torch.bfloat16)  # +2 ULP
+    assert bench.compare_outputs(got, want, "x")["ok"]
+    got[0, 6] = torch.tensor(1.0).to(torch.bfloat16).view(torch.int16).add(3).view(torch.bfloat16)  # +3 ULP
+    res = bench.compare_outputs(got, want, "x")
+    assert not res["ok"] and res["max_ulp_large_outputs"] == 3
+    got = want.clone()
+    got[1, 1] = -got[1, 1]                        # sign flip of a tiny value: far beyond 64 codes
+    res = bench.compare_outputs(got, want, "x")
+    assert not res["ok"] and res["beyond_64_ulp"] == 1 and res["max_ulp_large_outputs"] == 0
