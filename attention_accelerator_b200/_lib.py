@@ -30,6 +30,7 @@ GQA_ERR_UNSUPPORTED_DEVICE = 15
 GQA_ERR_ROPE_THETA = 16
 GQA_ERR_FLAGS = 17
 GQA_ERR_MEMORY = 18
+GQA_ERR_KV_HEADS = 19
 
 #: codes that describe a bad call configuration (the reference's config_error)
 CONFIG_ERRORS = {GQA_ERR_GEOMETRY, GQA_ERR_SEQ_LEN, GQA_ERR_N_KV_TILES, GQA_ERR_SCALE,
@@ -93,6 +94,9 @@ _SIGNATURES = {
                                             ctypes.c_int, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "gqa_decode": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), _P, ctypes.c_size_t, _P]),
     "gqa_decode_noalloc": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), _P]),
+    "gqa_workspace_bytes_heads": (ctypes.c_size_t, [ctypes.POINTER(GqaParams), ctypes.c_int]),
+    "gqa_decode_heads": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), ctypes.c_int, ctypes.c_int, _P,
+                                        ctypes.c_size_t, _P]),
     "gqa_decode_batched": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), ctypes.POINTER(GqaSeqDesc),
                                           _P, ctypes.c_int, _P, ctypes.c_size_t, _P]),
     "gqa_decode_chunked": (ctypes.c_int, [_P, _P, _P, _P, ctypes.POINTER(GqaParams), ctypes.POINTER(GqaChunkParams),

@@ -233,6 +233,59 @@ def decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, seq_len: int | 
     return dev_out
 
 
+def decode_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, kv_heads: tuple[int, int],
+                 seq_len: int | None = None, query_position: int | None = None,
+                 kv_block_len: int = DEFAULT_KV_BLOCK_LEN, scale: float | None = None,
+                 rope_theta: float = ROPE_THETA, out: torch.Tensor | None = None,
+                 k_rotated: bool = False) -> torch.Tensor:
+    """:func:`decode` of the KV heads ``kv_heads = (begin, count)`` only (C ABI
+    ``gqa_decode_heads``): each KV head and its 4 Q heads depend on no other head
+    (gqa_controller.v:159-162), so a sequence's heads can be sharded across GPUs
+    with no exchange.
+
+    ``q``: BF16 ``[32, 128]`` on this GPU (the Q rows of the range are read).
+    ``k``/``v``: BF16 ``[rows, count, 128]``, position-major, the range's heads
+    only.  Writes the range's rows of ``out`` (BF16 ``[32, 128]``, zeros
+    elsewhere when allocated here) and returns it.
+    """
+    lib = _lib.load()
+    begin, count = (int(x) for x in kv_heads)
+    if seq_len is None:
+        seq_len = k.shape[0]
+    p = make_params(seq_len=seq_len, query_position=query_position, kv_block_len=kv_block_len, scale=scale,
+                    rope_theta=rope_theta)
+    _check(lib.gqa_validate(ctypes.byref(p)), "decode_heads")
+    if k_rotated:
+        p.flags |= _lib.GQA_FLAG_K_ROTATED
+    if not q.is_cuda:
+        raise ValueError("decode_heads takes CUDA tensors")
+    device = q.device
+    if q.dtype != torch.bfloat16 or tuple(q.shape) != (N_Q_HEADS, HEAD_DIM) or q.stride(-1) != 1:
+        raise ValueError("q must be bfloat16 [32, 128] with a contiguous last dim")
+    for name, t in (("k", k), ("v", v)):
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or tuple(t.shape[1:]) != (count, HEAD_DIM) or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be bfloat16 [rows, {count}, {HEAD_DIM}] with a contiguous last dim")
+        if t.shape[0] < seq_len:
+            raise ValueError(f"{name} holds {t.shape[0]} rows, SEQ_LEN is {seq_len}")
+    _check_cuda(device, k=k, v=v)
+    p.k_pos_stride, p.k_head_stride = k.stride(0), k.stride(1)
+    p.v_pos_stride, p.v_head_stride = v.stride(0), v.stride(1)
+    if out is None:
+        out = torch.zeros((N_Q_HEADS, HEAD_DIM), dtype=torch.bfloat16, device=device)
+    else:
+        _check_out(out, (N_Q_HEADS, HEAD_DIM), torch.bfloat16, device)
+    _set_q_out(p, q, out, False)
+    stream = _stream_ptr(device)
+    nbytes = lib.gqa_workspace_bytes_heads(ctypes.byref(p), count)
+    if nbytes == 0:
+        raise GqaError(_lib.GQA_ERR_KV_HEADS if not 1 <= count <= N_KV_HEADS else _lib.GQA_ERR_CUDA,
+                       "decode_heads: workspace sizing failed")
+    ws = _workspace(device, stream, nbytes)
+    _check(lib.gqa_decode_heads(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), ctypes.byref(p), begin,
+                                count, ws.data_ptr(), ws.numel(), stream), "decode_heads")
+    return out
+
+
 def decode_chunked(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, first_position: int,
                    seq_len: int | None = None, kv_block_len: int = DEFAULT_KV_BLOCK_LEN,
                    scale: float | None = None, layout: str = "position_major", rope_theta: float = ROPE_THETA,

@@ -119,9 +119,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // 3-D tensor map over K or V: (head_dim, row, head) when rows are the smaller
 // stride (head-major), else (head_dim, head, row).  One box = one tile of
-// consecutive rows of one head; rows past `rows` read as zeros.
+// consecutive rows of one head; rows past `rows` read as zeros.  `heads`: the
+// KV heads the tensor holds (8, or a head-sharded call's range).
 int make_kv_map(CUtensorMap* map, const void* base, int64_t pos_stride, int64_t head_stride, int64_t rows,
-                int* rows_inner) {
+                int* rows_inner, int heads = gqa::kNumKVHeads) {
     PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (!encode) return GQA_ERR_CUDA;
     const cuuint64_t tile = (cuuint64_t)gqa::decode_tile_keys();
@@ -130,12 +131,12 @@ int make_kv_map(CUtensorMap* map, const void* base, int64_t pos_stride, int64_t 
     cuuint32_t box[3];
     const cuuint32_t estr[3] = {1, 1, 1};
     if (pos_stride <= head_stride) {
-        dims[0] = gqa::kHeadDim; dims[1] = (cuuint64_t)rows; dims[2] = gqa::kNumKVHeads;
+        dims[0] = gqa::kHeadDim; dims[1] = (cuuint64_t)rows; dims[2] = (cuuint64_t)heads;
         strides[0] = (cuuint64_t)pos_stride * 2; strides[1] = (cuuint64_t)head_stride * 2;
         box[0] = gqa::kHeadDim; box[1] = (cuuint32_t)tile; box[2] = 1;
         *rows_inner = 1;
     } else {
-        dims[0] = gqa::kHeadDim; dims[1] = gqa::kNumKVHeads; dims[2] = (cuuint64_t)rows;
+        dims[0] = gqa::kHeadDim; dims[1] = (cuuint64_t)heads; dims[2] = (cuuint64_t)rows;
         strides[0] = (cuuint64_t)head_stride * 2; strides[1] = (cuuint64_t)pos_stride * 2;
         box[0] = gqa::kHeadDim; box[1] = 1; box[2] = (cuuint32_t)tile;
         *rows_inner = 0;
@@ -236,15 +237,19 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 // <= 16 splits merged inside one cluster per KV head when the device holds all
 // 8 such clusters at once and that costs fewer tiles per CTA than the one-wave
 // plan with its last-split merge.
-Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = false, bool clusters_ok = true) {
-    const int slots = sms / gqa::kNumKVHeads > 0 ? sms / gqa::kNumKVHeads : 1;
+Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = false, bool clusters_ok = true,
+               int heads = gqa::kNumKVHeads) {
+    const int slots = sms / heads > 0 ? sms / heads : 1;
     int64_t total = 0, longest = 0;
     for (int b = 0; b < batch; ++b) {
         total += gqa::seq_key_count(d[b]);
         longest = std::max<int64_t>(longest, gqa::seq_key_count(d[b]));
     }
-    // The last split of a sequence stages every split's partial in shared memory.
-    const int64_t min_chunk = (longest + gqa::decode_max_splits() - 1) / gqa::decode_max_splits();
+    // The last split of a sequence stages every split's partial in shared memory;
+    // a single sequence stays within the in-kernel last-split merge (a KV-head
+    // subset on its own GPU would otherwise be cut into more splits than that).
+    const int max_splits = batch == 1 ? gqa::decode_last_merge_max_splits() : gqa::decode_max_splits();
+    const int64_t min_chunk = (longest + max_splits - 1) / max_splits;
     auto splits_for = [&](int chunk) {
         int64_t s = 0;
         for (int b = 0; b < batch; ++b) s += gqa::seq_splits(d[b], chunk);
@@ -291,7 +296,7 @@ Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = f
         if (chunk < floor_chunk) chunk = floor_chunk;
         if (chunk < min_chunk) chunk = min_chunk;
         const int c = round8(chunk);
-        const int64_t ctas = splits_for(c) * gqa::kNumKVHeads;
+        const int64_t ctas = splits_for(c) * heads;
         const int64_t waves = (ctas + sms - 1) / sms;
         const double cost = batch == 1 ? (double)waves * (double)(c + kOverheadKeys) : schedule_cost(c);
         if (best_chunk == 0 || cost < best_cost) {
@@ -308,7 +313,8 @@ Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = f
         // One split fewer per KV head when that costs no extra tile: the SMs it
         // frees take the next call's CTAs while this call's last splits merge.
         if (slots > 2) {
-            const int c = round8(std::max<int64_t>(kMinChunk, (longest + slots - 2) / (slots - 1)));
+            const int c = round8(std::max<int64_t>(std::max<int64_t>(kMinChunk, min_chunk),
+                                                   (longest + slots - 2) / (slots - 1)));
             if (tiles(c) == tiles(pl.chunk)) {
                 pl.chunk = c;
                 pl.total_splits = (int)splits_for(c);
@@ -319,7 +325,7 @@ Plan make_plan(const gqa::SeqDesc* d, int batch, int sms, bool allow_cluster = f
             const int c = round8(std::max<int64_t>(kMinChunk, (longest + n - 1) / n));
             const int ns = (int)splits_for(c);
             const double cost = tiles(c) + kClusterMergeTiles;
-            if (clusters_ok && ns >= 2 && cost < best && cluster_capacity(ns) >= gqa::kNumKVHeads) {
+            if (clusters_ok && ns >= 2 && cost < best && cluster_capacity(ns) >= heads) {
                 best = cost;
                 pl.chunk = c;
                 pl.total_splits = ns;
@@ -361,13 +367,13 @@ gqa::SeqDesc single_desc(const gqa_params* p) {
 }
 
 int fill_args(gqa::DecodeArgs& a, const void* q, const void* k, const void* v, void* out, const gqa_params* p,
-              void* ws, const Plan& pl, int batch) {
+              void* ws, const Plan& pl, int batch, int head0 = 0, int heads = gqa::kNumKVHeads) {
     std::memset(&a, 0, sizeof(a));
     if (pl.kv_rows > 0x7FFFFFFF) return GQA_ERR_KV_RANGE;
     int inner_k = 0, inner_v = 0;
-    int st = make_kv_map(&a.kmap, k, p->k_pos_stride, p->k_head_stride, pl.kv_rows, &inner_k);
+    int st = make_kv_map(&a.kmap, k, p->k_pos_stride, p->k_head_stride, pl.kv_rows, &inner_k, heads);
     if (st != GQA_OK) return st;
-    st = make_kv_map(&a.vmap, v, p->v_pos_stride, p->v_head_stride, pl.kv_rows, &inner_v);
+    st = make_kv_map(&a.vmap, v, p->v_pos_stride, p->v_head_stride, pl.kv_rows, &inner_v, heads);
     if (st != GQA_OK) return st;
     if (inner_k != inner_v) return GQA_ERR_ALIGNMENT;  // K and V must share one layout
     a.kv_rows_inner = inner_k;
@@ -394,6 +400,8 @@ int fill_args(gqa::DecodeArgs& a, const void* q, const void* k, const void* v, v
     a.mask_out = p->mask_out;
     a.mask_stride = p->mask_stride;
     a.kv_block_len = (int)p->kv_block_len;
+    a.head0 = head0;
+    a.n_heads = heads;
     bool out_of_slots = false;
     if (gqa::rope_table_for((double)p->rope_theta, &a.rope, &out_of_slots) != cudaSuccess) return GQA_ERR_CUDA;
     if (out_of_slots) return GQA_ERR_ROPE_THETA;
@@ -425,6 +433,7 @@ const char* gqa_status_string(int status) {
         case GQA_ERR_ROPE_THETA: return "invalid rope_theta, or more than 4 distinct rope_theta values on one device";
         case GQA_ERR_FLAGS: return "gqa_params.flags holds a bit this entry point does not support";
         case GQA_ERR_MEMORY: return "a tensor, table or workspace pointer is not memory of the current GPU";
+        case GQA_ERR_KV_HEADS: return "KV-head range is empty or outside [0, 8)";
         default: return "unknown status";
     }
 }
@@ -545,6 +554,45 @@ int gqa_decode(const void* q, const void* k, const void* v, void* out, const gqa
     if (st != GQA_OK) return st;
     gqa::DecodeArgs a;
     st = fill_args(a, q, k, v, out, p, workspace, pl, 1);
+    if (st != GQA_OK) return st;
+    a.descs = nullptr;
+    a.single = d;
+    a.cluster = pl.cluster;
+    if (pl.cluster == 0 && pl.total_splits > 1 && pl.total_splits <= gqa::decode_last_merge_max_splits())
+        a.ws_arrivals = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + kWsArrivalsOffset);
+    if (gqa::launch_decode(a, pl.total_splits, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return GQA_ERR_CUDA;
+    return GQA_OK;
+}
+
+size_t gqa_workspace_bytes_heads(const gqa_params* p, int kv_head_count) {
+    if (!p || gqa_validate(p) != GQA_OK) return 0;
+    if (kv_head_count < 1 || kv_head_count > gqa::kNumKVHeads) return 0;
+    int sms = 0;
+    if (current_device(&sms) != GQA_OK) return 0;
+    const gqa::SeqDesc d = single_desc(p);
+    return std::max(make_plan(&d, 1, sms, true, true, kv_head_count).ws_bytes,
+                    make_plan(&d, 1, sms, true, false, kv_head_count).ws_bytes);
+}
+
+int gqa_decode_heads(const void* q, const void* k, const void* v, void* out, const gqa_params* p,
+                     int kv_head_begin, int kv_head_count, void* workspace, size_t workspace_bytes, void* stream) {
+    int st = gqa_validate(p);
+    if (st != GQA_OK) return st;
+    if (kv_head_count < 1 || kv_head_begin < 0 || kv_head_begin + kv_head_count > gqa::kNumKVHeads)
+        return GQA_ERR_KV_HEADS;
+    st = check_layout(q, k, v, out, p);
+    if (st != GQA_OK) return st;
+    int sms = 0;
+    st = current_device(&sms);
+    if (st != GQA_OK) return st;
+    const gqa::SeqDesc d = single_desc(p);
+    const Plan pl = make_plan(&d, 1, sms, true, true, kv_head_count);
+    if (!workspace || !aligned16(workspace) || workspace_bytes < pl.ws_bytes) return GQA_ERR_WORKSPACE;
+    st = gqa::check_device_memory({workspace});
+    if (st != GQA_OK) return st;
+    gqa::DecodeArgs a;
+    st = fill_args(a, q, k, v, out, p, workspace, pl, 1, kv_head_begin, kv_head_count);
     if (st != GQA_OK) return st;
     a.descs = nullptr;
     a.single = d;

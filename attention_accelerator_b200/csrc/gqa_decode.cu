@@ -166,7 +166,7 @@ __device__ __forceinline__ void write_result4(const OutSpec& o, int b, int qh, i
 // and one for V (88 rows of one head, whatever the K/V strides) into the
 // shared-memory ring; returns once its copies have landed.
 __device__ __forceinline__ void produce_tiles(const DecodeArgs& a, uint8_t* smem, uint64_t* full, uint64_t* empty,
-                                             uint64_t* qbar, int b, int h, int64_t first_row, int n_tiles) {
+                                             uint64_t* qbar, int b, int h, int hm, int64_t first_row, int n_tiles) {
     const uint64_t pol = l2_evict_first_policy();
     // The group's Q rows go first, ahead of the K/V stream.
     mbar_arrive_expect_tx(qbar, kGroup * kRowBytes);
@@ -185,13 +185,9 @@ __device__ __forceinline__ void produce_tiles(const DecodeArgs& a, uint8_t* smem
         uint8_t* vd = kd + kTileBytes;
         mbar_arrive_expect_tx(&full[st], 2 * kTileBytes);
         const int row = static_cast<int>(first_row + (int64_t)t * kTileKeys);
-        if (a.kv_rows_inner) {
-            tma_load_3d(kd, &a.kmap, 0, row, h, &full[st], pol);
-            tma_load_3d(vd, &a.vmap, 0, row, h, &full[st], pol);
-        } else {
-            tma_load_3d(kd, &a.kmap, 0, h, row, &full[st], pol);
-            tma_load_3d(vd, &a.vmap, 0, h, row, &full[st], pol);
-        }
+        const int c1 = a.kv_rows_inner ? row : hm, c2 = a.kv_rows_inner ? hm : row;
+        tma_load_3d(kd, &a.kmap, 0, c1, c2, &full[st], pol);
+        tma_load_3d(vd, &a.vmap, 0, c1, c2, &full[st], pol);
         issued = t + 1;
     }
     if (!ok) atomicOr(a.ws_status, kDevStatusTimeout);
@@ -462,8 +458,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const int lane = threadIdx.x & 31;
     const int tid = threadIdx.x;
     const bool clustered = a.cluster > 0;  // grid (splits, heads), one cluster per head
-    const int h = clustered ? (int)blockIdx.y : (int)(blockIdx.x % kNumKVHeads);
-    const int gsplit = clustered ? (int)blockIdx.x : (int)(blockIdx.x / kNumKVHeads);
+    // KV head: h in the call's numbering (Q rows, output rows, partials,
+    // arrival counters), hm = h - head0 in the K/V tensor maps.
+    const int hm = clustered ? (int)blockIdx.y : (int)(blockIdx.x % a.n_heads);
+    const int h = a.head0 + hm;
+    const int gsplit = clustered ? (int)blockIdx.x : (int)(blockIdx.x / a.n_heads);
     const bool single = a.descs == nullptr;
 
     uint64_t* qbar = empty + kStages;
@@ -526,8 +525,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         for (int hq = 0; hq < kGroup; ++hq) bulk_prefetch_l2(a.q + (int64_t)(h * kGroup + hq) * a.q_hstride, kRowBytes);
         for (int t = 0; t < n_pre; ++t) {
             const int row = static_cast<int>(a.single.kv_start + key0 + (int64_t)t * kTileKeys);
-            tma_prefetch_3d(&a.kmap, 0, a.kv_rows_inner ? row : h, a.kv_rows_inner ? h : row);
-            tma_prefetch_3d(&a.vmap, 0, a.kv_rows_inner ? row : h, a.kv_rows_inner ? h : row);
+            tma_prefetch_3d(&a.kmap, 0, a.kv_rows_inner ? row : hm, a.kv_rows_inner ? hm : row);
+            tma_prefetch_3d(&a.vmap, 0, a.kv_rows_inner ? row : hm, a.kv_rows_inner ? hm : row);
         }
     }
     allow_dependent_launch();
@@ -614,13 +613,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const int64_t first_row = d.kv_start + key0;
 
     // The split merge finds each sequence's splits here.
-    if (!clustered && split == 0 && h == 0 && tid == 0 && n_split > 1) a.ws_seqinfo[b] = make_int2(lsplit, n_split);
+    if (!clustered && split == 0 && hm == 0 && tid == 0 && n_split > 1) a.ws_seqinfo[b] = make_int2(lsplit, n_split);
 
     // ======================= producer warp =======================
     // In a cluster the whole warp also takes part in the epilogue's two cluster
     // barriers.
     if (warp == kConsumerWarps) {
-        if (lane == 0) produce_tiles(a, smem, full, empty, qbar, b, h, first_row, n_tiles);
+        if (lane == 0) produce_tiles(a, smem, full, empty, qbar, b, h, hm, first_row, n_tiles);
         if (clustered) {
             __syncwarp();
             cluster_sync_all();  // partials published
@@ -631,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 
     // ======================= consumer warps =======================
     const int qpos = d.query_position;
-    if (a.mask_out != nullptr && split == 0 && h == 0) {
+    if (a.mask_out != nullptr && split == 0 && hm == 0) {
         const int n_pad = ((d.seq_len + a.kv_block_len - 1) / a.kv_block_len) * a.kv_block_len;
         for (int p = tid; p < n_pad; p += kConsumerThreads)
             a.mask_out[(int64_t)b * a.mask_stride + p] = key_valid(p, d.seq_len, qpos) ? 1 : 0;
@@ -929,14 +928,15 @@ struct MergeArgs {
     int single_splits;
     int chunk;
     OutSpec out;
+    int qh0, n_qh;          // the call's Q heads [qh0, qh0 + n_qh)
 };
 
 __global__ void __launch_bounds__(kHeadDim) split_merge_kernel(const __grid_constant__ MergeArgs m) {
     __shared__ float fac[kMaxSplitsPerSeq];
     __shared__ float red[2][4];
     allow_dependent_launch();
-    const int b = blockIdx.x / kNumQHeads;
-    const int qh = blockIdx.x % kNumQHeads;
+    const int b = blockIdx.x / m.n_qh;
+    const int qh = m.qh0 + (int)(blockIdx.x % m.n_qh);
     const int dim = threadIdx.x;
     grid_dependency_wait();
     const int n_split = m.descs == nullptr ? m.single_splits : seq_splits(m.descs[b], m.chunk);
@@ -1161,7 +1161,7 @@ cudaError_t decode_prepare(int device) {
 int decode_cluster_capacity(int cluster) {
     if (cluster < 2 || cluster > kMaxClusterSplits) return 0;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(cluster, kNumKVHeads);
+    cfg.gridDim = dim3(cluster, kNumKVHeads);  // the occupancy query counts clusters, whatever the grid
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmemBytes;
     cudaLaunchAttribute attr[1];
@@ -1184,8 +1184,8 @@ cudaError_t launch_decode(const DecodeArgs& a, int total_splits, cudaStream_t st
     const void* kern = (a.flags & GQA_FLAG_K_ROTATED) ? reinterpret_cast<const void*>(decode_kernel<true>)
                                                        : reinterpret_cast<const void*>(decode_kernel<false>);
     if (a.cluster > 0)  // single sequence, merged inside the clusters
-        return launch_pdl(kern, dim3(a.cluster, kNumKVHeads), dim3(kThreads), kSmemBytes, stream, dargs, a.cluster);
-    cudaError_t e = launch_pdl(kern, dim3(total_splits * kNumKVHeads), dim3(kThreads), kSmemBytes, stream, dargs);
+        return launch_pdl(kern, dim3(a.cluster, a.n_heads), dim3(kThreads), kSmemBytes, stream, dargs, a.cluster);
+    cudaError_t e = launch_pdl(kern, dim3(total_splits * a.n_heads), dim3(kThreads), kSmemBytes, stream, dargs);
     // Done when every sequence had one split or the last split of each head merged.
     if (e != cudaSuccess || total_splits <= a.batch || a.ws_arrivals != nullptr) return e;
     MergeArgs m;
@@ -1195,8 +1195,10 @@ cudaError_t launch_decode(const DecodeArgs& a, int total_splits, cudaStream_t st
     m.single_splits = a.descs == nullptr ? total_splits : 0;
     m.chunk = a.chunk;
     m.out = OutSpec{a.out, a.o_bstride, a.o_hstride, a.flags};
+    m.qh0 = a.head0 * kGroup;
+    m.n_qh = a.n_heads * kGroup;
     void* margs[] = {&m};
-    return launch_pdl(reinterpret_cast<const void*>(split_merge_kernel), dim3(a.batch * kNumQHeads), dim3(kHeadDim), 0,
+    return launch_pdl(reinterpret_cast<const void*>(split_merge_kernel), dim3(a.batch * m.n_qh), dim3(kHeadDim), 0,
                       stream, margs);
 }
 

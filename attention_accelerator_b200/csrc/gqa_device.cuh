@@ -107,6 +107,8 @@ struct alignas(64) DecodeArgs {
                             // (one arrival counter per KV head, zero between calls)
     const uint64_t* peer_bases;  // world > 1: this GPU decodes a shard of one sequence and exchanges the
     int world, rank;             // merged rows with the other ranks' exchange buffers (device array)
+    int head0, n_heads;     // KV heads [head0, head0 + n_heads) only; the K/V maps then hold just those
+                            // heads (map head index = h - head0).  0 and 8 for a whole call.
 };
 
 // Exchange buffer of the long-context split (one per rank, mapped by the others):

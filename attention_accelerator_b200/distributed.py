@@ -1,7 +1,12 @@
 """Multi-GPU plumbing for the decode path: one process per GPU over torch.distributed.
 
-Two schemes:
+Three schemes:
 
+* **KV-head sharding (no collective).**  One sequence's 8 KV heads are split
+  across ranks by :func:`head_range`; each rank holds the K/V rows of its heads
+  only and decodes them with ``decode_heads`` (a KV head and its 4 Q heads
+  depend on no other head, gqa_controller.v:159-162); the output rows are
+  disjoint.
 * **Sequence sharding (no collective).**  A batch of decode requests is split
   across ranks by :func:`balance_sequences` (greedy longest-first assignment
   by visible-key count); every rank decodes its own sequences.
@@ -36,6 +41,16 @@ def shard_range(n_keys: int, rank: int, world: int) -> tuple[int, int]:
     base, extra = divmod(n_keys, world)
     lo = rank * base + min(rank, extra)
     return lo, lo + base + (1 if rank < extra else 0)
+
+
+def head_range(rank: int, world: int, n_kv_heads: int = 8) -> tuple[int, int]:
+    """KV heads ``(begin, count)`` of ``rank`` when a sequence's ``n_kv_heads``
+    heads are sharded over ``world`` ranks (counts differ by <= 1; every rank gets
+    at least one, so ``world`` <= ``n_kv_heads``)."""
+    if not 1 <= world <= n_kv_heads:
+        raise ValueError(f"world must be in [1, {n_kv_heads}] to shard {n_kv_heads} KV heads")
+    lo, hi = shard_range(n_kv_heads, rank, world)
+    return lo, hi - lo
 
 
 def balance_sequences(visible_keys, world: int) -> list[list[int]]:

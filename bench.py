@@ -279,6 +279,86 @@ class SingleDecode(Workload):
         return self.out.view(self.torch.int16).cpu().numpy().astype(np.uint16)
 
 
+class HeadShardDecode(Workload):
+    """`--shard heads`: one config-1/2 sequence per step with its 8 KV heads
+    sharded over the ranks (distributed.head_range): every rank holds the K/V
+    rows of its heads only and decodes them with decode_heads, no collective.
+    Strong scaling (one sequence per step for the whole job)."""
+
+    def __init__(self, device, rank, world, seq_len, qpos, seed=20260805):
+        import torch
+        import attention_accelerator_b200 as gqa
+        from attention_accelerator_b200.distributed import head_range
+        self.gqa, self.torch = gqa, torch
+        self.S, self.qpos = seq_len, qpos
+        self.world = world
+        self.begin, self.count = head_range(rank, world)
+        self.name = f"config2_heads_s{seq_len}"
+        self.scaling = "strong"
+        self.bytes_per_step = kv_bytes(qpos + 1)  # the whole sequence, all ranks together
+        self.qheads_per_step = 32
+        per_set = 2 * seq_len * self.count * 128 * 2
+        self.nsets = max(2, math.ceil(2 * L2_BYTES / per_set))
+        g = torch.Generator(device=device).manual_seed(seed)  # the same sequences on every rank
+        self.q, self.kfull, self.vfull, self.k, self.v = [], [], [], [], []
+        b, c = self.begin, self.count
+        for _ in range(self.nsets):
+            self.q.append(torch.randn((32, 128), generator=g, device=device).to(torch.bfloat16))
+            kf = torch.randn((seq_len, 8, 128), generator=g, device=device).to(torch.bfloat16)
+            vf = torch.randn((seq_len, 8, 128), generator=g, device=device).to(torch.bfloat16)
+            self.k.append(kf[:, b:b + c].contiguous())
+            self.v.append(vf[:, b:b + c].contiguous())
+            self.kfull.append(kf)
+            self.vfull.append(vf)
+        self.out = torch.zeros((32, 128), dtype=torch.bfloat16, device=device)
+        self.graph_ok = True
+        # decode_kernel, plus split_merge_kernel when a head's splits exceed the in-kernel merge
+        self.launches_per_step = 1
+        self.l2_note = (f"{self.nsets} rotating buffer sets of {per_set / 2**20:.1f} MiB per rank "
+                        f"({self.nsets * per_set / 2**20:.0f} MiB > 2x L2)")
+
+    @property
+    def sets(self):
+        return self.nsets
+
+    def launch(self, i):
+        j = i % self.nsets
+        self.gqa.decode_heads(self.q[j], self.k[j], self.v[j], kv_heads=(self.begin, self.count), seq_len=self.S,
+                              query_position=self.qpos, out=self.out, k_rotated=self.k_rotated)
+
+    def check(self, steps: int) -> dict:
+        """This rank's rows of the last timed step against a single-GPU decode of
+        the whole sequence (all 8 heads) on this rank."""
+        j = (steps - 1) % self.nsets
+        want = self.gqa.decode(self.q[j], self.kfull[j], self.vfull[j], seq_len=self.S, query_position=self.qpos,
+                               k_rotated=self.k_rotated)
+        rows = slice(4 * self.begin, 4 * (self.begin + self.count))
+        return compare_outputs(self.out[rows], want[rows],
+                               "single-GPU decode of the whole sequence (this rank's heads' rows)")
+
+    def config(self):
+        return {"workload": self.name, "batch": 1, "seq_len": self.S, "query_position": self.qpos,
+                "kv_layout": f"position_major [S,{self.count},128] bf16: KV heads {self.begin}.."
+                             f"{self.begin + self.count - 1} on this rank",
+                "parallelism": f"KV-head sharding x{self.world} (decode_heads, no collective)",
+                "l2": self.l2_note}
+
+    def e2e_inputs(self):
+        return [x.cpu().pin_memory() for x in (self.q[0], self.k[0], self.v[0])]
+
+    def e2e_step(self, host):
+        dev = self.out.device
+        q, k, v = (x.to(dev, non_blocking=True) for x in host)
+        return self.gqa.decode_heads(q, k, v, kv_heads=(self.begin, self.count), seq_len=self.S,
+                                     query_position=self.qpos, k_rotated=self.k_rotated).cpu()
+
+    def oracle_inputs(self):
+        return None
+
+    def gpu_result_set0(self):
+        return None
+
+
 class RaggedBatch(Workload):
     """64 sequences, SEQ_LEN ~ U{512..8192}, K with outlier channels."""
 
@@ -735,9 +815,14 @@ def mem_cpu_run_parallel(budget_s: float, lines_per_proc: int = 16384):
             f"one spawned process each, {dt:.1f} s")
 
 
-def make_workload(name, device, rank, world, layout="position_major", chunk_batch=16, exchange="fused"):
+def make_workload(name, device, rank, world, layout="position_major", chunk_batch=16, exchange="fused",
+                  shard="sequences"):
     if name == "memcodec":
         return MemCodec(device, rank, world)
+    if shard == "heads":
+        if name != "config2":
+            raise SystemExit("--shard heads applies to config2 (one sequence's KV heads over the GPUs)")
+        return HeadShardDecode(device, rank, world, 4096, 4095)
     if name == "config1":
         return SingleDecode(device, rank, 30, 29, uniform=True, layout=layout)
     if name == "config2":
@@ -815,6 +900,26 @@ def traffic_for(workload: str, bytes_per_launch: float):
     if abs(alg - bytes_per_launch) > 1e-3 * bytes_per_launch:
         return None
     return rec.get("dram_bytes_per_launch")
+
+
+def box_hbm_copy_gbs(torch, device, elems: int = 1 << 28, reps: int = 5) -> float:
+    """This box's device-to-device copy rate (read + write bytes, best of `reps`,
+    CUDA events), measured the way the driver measures the HBM peak, but on the
+    GPU this run got: GPUs of the pool differ, and the kernel's fraction of this
+    figure separates the kernel from the box."""
+    a = torch.empty(elems, dtype=torch.bfloat16, device=device)
+    b = torch.empty_like(a)
+    b.copy_(a)
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        b.copy_(a)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) * 1e-3)
+    del a, b
+    return 2 * elems * 2 / best / 1e9
 
 
 def pinned_h2d_gbs(torch, nbytes: int, device, reps: int = 20) -> float:
@@ -1037,6 +1142,9 @@ def main():
                          "over peer memory (peer), or NCCL all-gather + combine (nccl)")
     ap.add_argument("--k-rotated", action="store_true",
                     help="configs 1-4: K cache stored pre-rotated (GQA_FLAG_K_ROTATED); decode rotates only Q")
+    ap.add_argument("--shard", choices=("sequences", "heads"), default="sequences",
+                    help="config2 at N>1: every GPU its own sequences (sequences), or one sequence's 8 KV heads "
+                         "split over the GPUs (heads)")
     ap.add_argument("--chunk-batch", type=int, default=16,
                     help="config5 sequences (16 is the BASELINE config; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -1060,7 +1168,7 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
         build_library()
-    wl = make_workload(args.workload, device, rank, world, args.layout, args.chunk_batch, args.exchange)
+    wl = make_workload(args.workload, device, rank, world, args.layout, args.chunk_batch, args.exchange, args.shard)
     if args.k_rotated:
         if args.workload not in ("config1", "config2", "config3", "config4"):
             raise SystemExit("--k-rotated applies to the decode workloads config1-4")
@@ -1107,6 +1215,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(wl, args.cpu_budget)
 
+    box_copy = box_hbm_copy_gbs(torch, device)
     traffic = traffic_for(wl.name, per_gpu_bytes)
     if wl.bound == "tensor":
         tpeak, tkind = peak_bf16()
@@ -1121,7 +1230,8 @@ def main():
     else:
         roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "peak_kind": peak_kind,
                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-                    "algorithmic_bytes_per_launch": per_gpu_bytes}
+                    "algorithmic_bytes_per_launch": per_gpu_bytes,
+                    "box_copy_gbs": round(box_copy, 1), "frac_of_box_copy": round(achieved / box_copy, 4)}
     if rank == 0:
         line = {
             "metric": getattr(wl, "metric", METRIC), "value": round(value, 2), "unit": getattr(wl, "unit", UNIT), "n_gpus": world, "steps": args.steps,

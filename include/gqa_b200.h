@@ -57,8 +57,9 @@ enum gqa_status {
     GQA_ERR_UNSUPPORTED_DEVICE = 15, /* current device is not sm_100 */
     GQA_ERR_ROPE_THETA = 16,       /* rope_theta <= 0, not finite, or a 5th distinct value on one device */
     GQA_ERR_FLAGS = 17,            /* gqa_params.flags holds a bit this entry point does not know */
-    GQA_ERR_MEMORY = 18            /* a tensor, table or workspace pointer is not memory of the current
+    GQA_ERR_MEMORY = 18,           /* a tensor, table or workspace pointer is not memory of the current
                                       GPU (host memory, pageable or pinned, or another GPU's memory) */
+    GQA_ERR_KV_HEADS = 19          /* KV-head range empty or outside [0, 8) (gqa_decode_heads) */
 };
 
 /* GQA_FLAG_* values for gqa_params.flags. */
@@ -207,6 +208,23 @@ int gqa_decode(const void *q, const void *k, const void *v, void *out,
                const gqa_params *p, void *workspace, size_t workspace_bytes, void *stream);
 
 /*
+ * gqa_decode of the KV heads [kv_head_begin, kv_head_begin + kv_head_count)
+ * only, and of their Q heads 4h .. 4h+3 (the GQA mapping of
+ * gqa_controller.v:159-162: a KV head and its Q group depend on no other head).
+ * For a sequence whose KV heads are sharded across GPUs: each GPU holds the K/V
+ * rows of its heads only and decodes them with the whole GPU, with no exchange.
+ *  - k, v: kv_head_count heads (head index h - kv_head_begin in the strides).
+ *  - q, out: the full 32-head layout; only the range's Q rows are read and only
+ *    its output rows written.
+ *  - workspace: gqa_workspace_bytes_heads(p, kv_head_count) bytes, header
+ *    zeroed as for gqa_decode.
+ * Returns GQA_ERR_KV_HEADS for an empty range or one outside [0, 8).
+ */
+size_t gqa_workspace_bytes_heads(const gqa_params *p, int kv_head_count);
+int gqa_decode_heads(const void *q, const void *k, const void *v, void *out, const gqa_params *p,
+                     int kv_head_begin, int kv_head_count, void *workspace, size_t workspace_bytes, void *stream);
+
+/*
  * gqa_decode without a workspace argument: no counterpart in the reference.
  * For callers that may not allocate device memory (a plug-in inside a host
  * program that owns every device allocation, or a loop that cannot afford
@@ -215,10 +233,20 @@ int gqa_decode(const void *q, const void *k, const void *v, void *out,
  * loads the library holds that array until the process exits.  Nothing is
  * allocated or freed by this call.
  *  - The first call on a device looks up the array's device address for that
- *    device (cudaGetSymbolAddress); make that first call before any stream
- *    capture begins.
+ *    device (cudaGetSymbolAddress), and the first call on a device with a
+ *    given rope_theta uploads that theta's RoPE table with a synchronous
+ *    cudaMemcpy, as gqa_decode does: such a first call synchronises the
+ *    device.  Make it before any stream capture begins and outside
+ *    latency-critical loops; later calls synchronise nothing.
+ *  - The address is kept for the life of the process: after a
+ *    cudaDeviceReset on a device that has used this entry point, do not call
+ *    it again on that device.
  *  - A call whose scratch would exceed GQA_NOALLOC_SCRATCH_BYTES returns
  *    GQA_ERR_WORKSPACE without launching; use gqa_decode with a workspace.
+ *    A single sequence is cut into at most one wave of splits (8 CTAs each)
+ *    and at most 32 splits, so it needs at most 512 + min(SMs / 8, 32) x
+ *    16,896 bytes: 0.3 MiB on a 148-SM B200, 0.54 MiB on any GPU, so this
+ *    refusal is a guard that valid calls do not reach.
  *  - All calls on a device share the one array and it keeps the last call's
  *    contents: calls whose kernels overlap on the GPU (several streams, or
  *    several host threads) race and corrupt each other's results; serialise

@@ -18,7 +18,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from attention_accelerator_b200.distributed import balance_sequences, gather_partials, shard_range
+from attention_accelerator_b200.distributed import balance_sequences, gather_partials, head_range, shard_range
 
 
 def _free_port() -> int:
@@ -71,6 +71,58 @@ def test_sequence_split_over_gloo_matches_single_process(seq_len, qpos):
         res = check_rows(golden, results[r], 64)
         assert res.passed and res.worst_ulp <= 1, res.line()
     np.testing.assert_array_equal(results[0], results[1])
+
+
+def _head_worker(rank: int, world: int, port: int, seq_len: int, result_q):
+    """One rank of a KV-head-sharded decode: the golden of its heads only (K/V of
+    those heads, their Q rows), then an all-gather of the output rows."""
+    from oracle.golden import gqa_golden_f64
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, k, v = _inputs(seq_len, seed=11)
+        begin, count = head_range(rank, world)
+        mine = gqa_golden_f64(q[4 * begin:4 * (begin + count)], k[begin:begin + count], v[begin:begin + count],
+                              seq_len, seq_len - 1, exact=False)
+        rows = torch.zeros((32, 128), dtype=torch.float64)
+        rows[4 * begin:4 * (begin + count)] = torch.from_numpy(mine)
+        gathered = [torch.zeros_like(rows) for _ in range(world)]
+        dist.all_gather(gathered, rows)
+        result_q.put((rank, sum(gathered).numpy()))  # disjoint rows: the sum assembles them
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_sharding_over_gloo_matches_single_process():
+    """KV heads split over 2 ranks with no exchange of partial results: the
+    assembled rows equal the single-process golden bit for bit."""
+    from oracle.golden import gqa_golden_f64
+    world, seq_len = 2, 200
+    ctx = mp.get_context("spawn")
+    result_q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_head_worker, args=(r, world, port, seq_len, result_q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(result_q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    q, k, v = _inputs(seq_len, seed=11)
+    golden = gqa_golden_f64(q, k, v, seq_len, seq_len - 1, exact=False)
+    for r in range(world):
+        np.testing.assert_array_equal(results[r], golden)
+
+
+def test_head_ranges_partition_the_kv_heads():
+    for world in range(1, 9):
+        ranges = [head_range(r, world) for r in range(world)]
+        heads = [h for b, c in ranges for h in range(b, b + c)]
+        assert heads == list(range(8))
+        assert min(c for _, c in ranges) >= 1 and max(c for _, c in ranges) - min(c for _, c in ranges) <= 1
+    for bad in (0, 9):
+        with pytest.raises(ValueError):
+            head_range(0, bad)
 
 
 def test_shard_ranges_cover_exactly():

@@ -392,3 +392,18 @@ def test_bench_output_check_counts_ulps_like_the_reference():
     got[1, 1] = -got[1, 1]                        # sign flip of a tiny value: far beyond 64 codes
     res = bench.compare_outputs(got, want, "x")
     assert not res["ok"] and res["beyond_64_ulp"] == 1 and res["max_ulp_large_outputs"] == 0
+
+
+def test_decode_heads_refuses_bad_head_ranges_before_any_gpu_work():
+    """gqa_decode_heads checks the KV-head range on the host (GQA_ERR_KV_HEADS),
+    after the register checks and before touching any pointer or device."""
+    import ctypes
+    from attention_accelerator_b200.api import make_params
+    lib = _lib.load()
+    p = make_params(seq_len=64)
+    for begin, count in ((0, 0), (-1, 2), (7, 2), (0, 9), (8, 1)):
+        st = lib.gqa_decode_heads(None, None, None, None, ctypes.byref(p), begin, count, None, 0, None)
+        assert st == _lib.GQA_ERR_KV_HEADS, (begin, count, st)
+    bad = make_params(seq_len=64, n_q_heads=31)
+    assert lib.gqa_decode_heads(None, None, None, None, ctypes.byref(bad), 0, 1, None, 0, None) == _lib.GQA_ERR_GEOMETRY
+    assert lib.gqa_workspace_bytes_heads(ctypes.byref(p), 0) == 0
