@@ -444,6 +444,9 @@ class LongContext(Workload):
         self.S = seq_len
         self.name = f"config4_decode_s{seq_len}"
         self.scaling = "strong"
+        if world == 1:  # what bounds the single-GPU step (ncu; profiles/decode_kernel_config4_s131072.md)
+            self.limiter = ("one decode_kernel launch: a latency-bound consumer loop at 12 warps per SM "
+                            "(issue ~52 % active, FMA pipe ~51 %, DRAM traffic 1.009x algorithmic)")
         self.bytes_per_step = kv_bytes(seq_len)  # whole job; each rank reads 1/world of the keys
         self.qheads_per_step = 32
         from attention_accelerator_b200.distributed import shard_range
@@ -1201,6 +1204,10 @@ def main():
     if breakdown:
         breakdown["step_us"] = round(ms_step * 1e3, 3)
         breakdown["exchange_and_merge_us"] = round(breakdown["step_us"] - breakdown["shard_decode_us"], 3)
+        breakdown["limiter"] = ("the shard decode" if breakdown["exchange_and_merge_us"] < breakdown["shard_decode_us"]
+                                else "the exchange and merge") + " (the larger part of the step)"
+    elif getattr(wl, "limiter", None):
+        breakdown = {"limiter": wl.limiter}
     e2e_dt, h2d, d2h = e2e_run(torch, wl, args.e2e_steps, device)
     copy_gbs = pinned_h2d_gbs(torch, h2d, device)
     if dist_on:
