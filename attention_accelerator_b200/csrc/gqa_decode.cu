@@ -264,97 +264,91 @@ constexpr int kLastMergeScratchFloats = kGroup * kLastMergeMaxSplits + 2 * kGrou
 
 // Long-context split across GPUs, fused into the decode: the CTA that holds
 // this rank's merged rows of Q heads 4h..4h+3 (acc[128], m, l in shared
-// memory) pushes them into every rank's exchange buffer (push_rows[e & 1][rank],
-// plain stores over NVLink), releases them at system scope with one flag per
-// (source rank, KV head) = e in each destination, then waits (bounded) for the
-// peers' flags of head h in its OWN buffer and merges the rows it received,
+// memory) pushes them into every rank's exchange buffer
+// (push_rows[e & 1][rank]) as 64-bit words that each carry the value and the
+// epoch e: one NVLink write per word carries its own flag, so the data needs
+// no fence and no separate flag store.  Each thread then polls, in its OWN
+// buffer (bounded), the words of the outputs it merges, for every source
+// rank, and merges
 //   M = max m_r, O = sum 2^(m_r - M) acc_r, L = sum 2^(m_r - M) l_r,
-// writing BF16 O / L; the last of the eight heads advances the epoch.  Pushing
-// puts one one-way NVLink transfer on the critical path instead of remote
-// polling and remote reads.  Rows of epoch e are rewritten at e + 2 only: by
-// then every peer has published e + 1, which it does after finishing epoch e.
+// writing BF16 O / L; the last of the eight heads advances the epoch.  Rows of
+// epoch e are rewritten at e + 2 only: by then every peer has published e + 1,
+// which it does after finishing epoch e; a stale word carries e - 2 and is
+// never mistaken for e.
+__device__ __forceinline__ void st_word_sys(uint64_t* p, float v, uint32_t e) {
+    const uint64_t w = ((uint64_t)e << 32) | (uint64_t)__float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_word_sys(const uint64_t* p) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// The value of word p once it carries epoch e (bounded wait; ok turns false on expiry and stays false).
+__device__ __forceinline__ float wait_word(const uint64_t* p, uint32_t e, bool& ok) {
+    uint64_t w = ld_word_sys(p);
+    if ((uint32_t)(w >> 32) != e && ok) {
+        const long long t0 = clock64();
+        do {
+            w = ld_word_sys(p);
+            if (clock64() - t0 > kWaitTimeoutCycles) {
+                ok = false;
+                break;
+            }
+        } while ((uint32_t)(w >> 32) != e);
+    }
+    return __uint_as_float((uint32_t)w);
+}
+
 __device__ __forceinline__ void exchange_and_finish(const DecodeArgs& a, int h, int tid, const float* rows,
                                                     int* info, const OutSpec& direct) {
     uint8_t* mine = reinterpret_cast<uint8_t*>(a.peer_bases[a.rank]);
     uint32_t* hdr = reinterpret_cast<uint32_t*>(mine);
     const size_t push = peer_push_offset(1);
-    if (tid == 0) {
-        info[3] = (int)(*reinterpret_cast<volatile uint32_t*>(hdr) + 1u);
-        info[4] = 1;  // cleared by a wait that gives up
-    }
+    if (tid == 0) info[3] = (int)(*reinterpret_cast<volatile uint32_t*>(hdr) + 1u);
     named_barrier_sync(1, kConsumerThreads);
     const uint32_t e = (uint32_t)info[3];
-    // Row (source rank r, Q head 4h + hq) of parity e & 1 in any rank's push area.
+    // Words of (source rank r, Q head 4h + hq) of parity e & 1 in any rank's push area.
     auto push_row = [&](uint8_t* base, int r) {
-        return reinterpret_cast<float*>(base + push + kPushFlagsBytes) +
-               (((size_t)(e & 1u) * kMaxPeers + r) * kNumQHeads + (size_t)h * kGroup) * kPartialFloats;
+        return reinterpret_cast<uint64_t*>(base + push + kPushFlagsBytes) +
+               (((size_t)(e & 1u) * kMaxPeers + r) * kNumQHeads + (size_t)h * kGroup) * kPushRowWords;
     };
     for (int p = 0; p < a.world; ++p) {
-        float* dst = push_row(reinterpret_cast<uint8_t*>(a.peer_bases[p]), a.rank);
-        for (int i = tid; i < kGroup * kPartialFloats; i += kConsumerThreads) dst[i] = rows[i];
+        uint64_t* dst = push_row(reinterpret_cast<uint8_t*>(a.peer_bases[p]), a.rank);
+        for (int i = tid; i < kGroup * kPushRowWords; i += kConsumerThreads)
+            st_word_sys(dst + i, rows[(i / kPushRowWords) * kPartialFloats + i % kPushRowWords], e);
     }
-    named_barrier_sync(1, kConsumerThreads);
-    if (tid == 0) {
-        // One system-scope release for all peers: the fence orders every push
-        // (ours, and the CTA's through the barrier above) before the flag
-        // stores, which then go out back to back instead of one NVLink round
-        // trip per peer.
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        for (int p = 0; p < a.world; ++p) {
-            uint32_t* flags = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(a.peer_bases[p]) + push);
-            st_relaxed_sys(flags + a.rank * kNumKVHeads + h, e);
-        }
-    }
-    // Thread r waits for source rank r's flag of head h in this rank's own buffer.
-    if (tid < a.world) {
-        const uint32_t* flag = reinterpret_cast<const uint32_t*>(mine + push) + tid * kNumKVHeads + h;
-        int ok = 1;
-        if ((int)(ld_acquire_sys(flag) - e) < 0) {
-            const long long t0 = clock64();
-            while ((int)(ld_acquire_sys(flag) - e) < 0) {
-                if (clock64() - t0 > kWaitTimeoutCycles) {
-                    ok = 0;
-                    break;
-                }
+    bool ok = true;
+    for (int o = tid; o < kOutputs; o += kConsumerThreads) {
+        const int hq = o >> 7, dim = o & 127;
+        float mr[kMaxPeers], lr[kMaxPeers], ar[kMaxPeers];
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) {
+            if (r < a.world) {
+                const uint64_t* row = push_row(mine, r) + hq * kPushRowWords;
+                mr[r] = wait_word(row + kHeadDim, e, ok);
+                lr[r] = wait_word(row + kHeadDim + 1, e, ok);
+                ar[r] = wait_word(row + dim, e, ok);
             }
         }
-        if (!ok) {
-            atomicOr(a.ws_status, kDevStatusTimeout);
-            info[4] = 0;
-        }
-    }
-    named_barrier_sync(1, kConsumerThreads);
-    const bool all_ok = info[4] != 0;
-    if (all_ok) {
-        for (int o = tid; o < kOutputs; o += kConsumerThreads) {
-            const int hq = o >> 7, dim = o & 127;
-            float mr[kMaxPeers], lr[kMaxPeers], ar[kMaxPeers];
+        if (!ok) break;
+        float M = -INFINITY;
 #pragma unroll
-            for (int r = 0; r < kMaxPeers; ++r) {
-                if (r < a.world) {
-                    const volatile float* row = push_row(mine, r) + hq * kPartialFloats;
-                    mr[r] = row[kHeadDim];
-                    lr[r] = row[kHeadDim + 1];
-                    ar[r] = row[dim];
-                }
+        for (int r = 0; r < kMaxPeers; ++r)
+            if (r < a.world) M = fmaxf(M, mr[r]);
+        const float Mu = M == -INFINITY ? 0.f : M;
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) {
+            if (r < a.world) {
+                const float f = exp2f(mr[r] - Mu);
+                L = fmaf(lr[r], f, L);
+                O = fmaf(ar[r], f, O);
             }
-            float M = -INFINITY;
-#pragma unroll
-            for (int r = 0; r < kMaxPeers; ++r)
-                if (r < a.world) M = fmaxf(M, mr[r]);
-            const float Mu = M == -INFINITY ? 0.f : M;
-            float L = 0.f, O = 0.f;
-#pragma unroll
-            for (int r = 0; r < kMaxPeers; ++r) {
-                if (r < a.world) {
-                    const float f = exp2f(mr[r] - Mu);
-                    L = fmaf(lr[r], f, L);
-                    O = fmaf(ar[r], f, O);
-                }
-            }
-            write_result(direct, 0, h * kGroup + hq, dim, O, M, L);
         }
+        write_result(direct, 0, h * kGroup + hq, dim, O, M, L);
     }
+    if (!ok) atomicOr(a.ws_status, kDevStatusTimeout);
     if (tid == 0) {
         __threadfence();
         if (atomicAdd(hdr + 1, 1u) == (uint32_t)(kNumKVHeads - 1)) {

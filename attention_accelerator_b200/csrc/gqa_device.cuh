@@ -116,8 +116,8 @@ struct alignas(64) DecodeArgs {
 //   float rows[2][batch * 32][132] from peer_data_offset(batch), double-buffered by epoch
 //   parity: the pull exchange of gqa_combine_peers (each rank publishes into its own buffer);
 //   then, from peer_push_offset(batch), the push exchange of the fused decode (one sequence):
-//   u32 push_flag[kMaxPeers][8 KV heads] and float push_rows[2][kMaxPeers][32][132], which
-//   the ranks write into each other's buffers.
+//   256 bytes (kPushFlagsBytes, unused by the word protocol) and u64 push_rows[2][kMaxPeers][32][130],
+//   each word (epoch << 32 | value bits), which the ranks write into each other's buffers.
 constexpr int kPeerFlagsOffset = 64;
 constexpr int kMaxPeers = 8;
 __host__ __device__ inline size_t peer_data_offset(int batch) {
@@ -128,7 +128,10 @@ __host__ __device__ inline size_t peer_push_offset(int batch) {
     return peer_data_offset(batch) + 2 * (size_t)batch * kNumQHeads * kPartialFloats * sizeof(float);
 }
 constexpr size_t kPushFlagsBytes = 256;  // kMaxPeers x 8 KV heads x u32
-constexpr size_t kPushRowsBytes = 2 * (size_t)kMaxPeers * kNumQHeads * kPartialFloats * sizeof(float);
+// Push rows of the fused exchange: [2 parities][kMaxPeers source ranks][32 Q heads][130] 64-bit words,
+// each (value, epoch): acc[128], m, l.
+constexpr int kPushRowWords = kHeadDim + 2;
+constexpr size_t kPushRowsBytes = 2 * (size_t)kMaxPeers * kNumQHeads * kPushRowWords * sizeof(uint64_t);
 static_assert(kMaxPeers * kNumKVHeads * 4 <= (int)kPushFlagsBytes, "push flags fit");
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {

@@ -8,8 +8,9 @@ call on rank 1's buffer publishes its rows before rank 0's world-size-2 call.
 gqa_decode_exchange pushes rows into every rank's buffer, so rank 1's call runs
 first: it pushes its rows into rank 0's buffer, and its own wait for rank 0
 gives up after ~1 s and reports it.  Rank 0's call then finds the rows.  The
-timeout tests leave a peer flag unset and check that the bounded wait gives up
-and reports it.  The two-process test (2 GPUs) runs the real IPC-mapped
+timeout tests leave a peer's flag (combine) or words (decode exchange, whose
+pushed values carry their epoch) unwritten and check that the bounded wait
+gives up and reports it.  The two-process test (2 GPUs) runs the real IPC-mapped
 exchange with torch.distributed ranks.
 """
 from __future__ import annotations
