@@ -401,7 +401,9 @@ int gqa_combine_peers(const float *partials, int64_t partial_batch_stride, const
  * rows to the exchange buffer, waits for the peers' rows over NVLink and writes
  * the final BF16 rows of the whole sequence to `out` [32][128] on every rank —
  * one launch per step, no combine kernel.  The rows are pushed into every
- * rank's buffer and each rank waits on flags in its own memory.  2 <= world <= 8.
+ * rank's buffer as 64-bit words that carry the step's epoch beside each value,
+ * and each rank waits (bounded) on those words in its own memory.
+ * 2 <= world <= 8.
  * `workspace`: gqa_workspace_bytes(p, shard, 1) bytes (the 256-byte header zeroed
  * at allocation).  p->flags must be 0.  The exchange buffers are those of
  * gqa_peer_buffer_create (batch 1).
