@@ -284,9 +284,9 @@ __device__ __forceinline__ uint64_t ld_word_sys(const uint64_t* p) {
     asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
-// The value of word p once it carries epoch e (bounded wait; ok turns false on expiry and stays false).
-__device__ __forceinline__ float wait_word(const uint64_t* p, uint32_t e, bool& ok) {
-    uint64_t w = ld_word_sys(p);
+// Word p as first loaded (`w`), or once it carries epoch e: a bounded wait only
+// for a word that had not arrived yet; ok turns false on expiry and stays false.
+__device__ __forceinline__ float word_value(uint64_t w, const uint64_t* p, uint32_t e, bool& ok) {
     if ((uint32_t)(w >> 32) != e && ok) {
         const long long t0 = clock64();
         do {
@@ -321,14 +321,26 @@ __device__ __forceinline__ void exchange_and_finish(const DecodeArgs& a, int h, 
     bool ok = true;
     for (int o = tid; o < kOutputs; o += kConsumerThreads) {
         const int hq = o >> 7, dim = o & 127;
+        // All 3 x world words are loaded before any is examined, so their
+        // latencies overlap; only a word that has not arrived is polled again.
+        uint64_t wm[kMaxPeers], wl[kMaxPeers], wa[kMaxPeers];
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r) {
+            if (r < a.world) {
+                const uint64_t* row = push_row(mine, r) + hq * kPushRowWords;
+                wm[r] = ld_word_sys(row + kHeadDim);
+                wl[r] = ld_word_sys(row + kHeadDim + 1);
+                wa[r] = ld_word_sys(row + dim);
+            }
+        }
         float mr[kMaxPeers], lr[kMaxPeers], ar[kMaxPeers];
 #pragma unroll
         for (int r = 0; r < kMaxPeers; ++r) {
             if (r < a.world) {
                 const uint64_t* row = push_row(mine, r) + hq * kPushRowWords;
-                mr[r] = wait_word(row + kHeadDim, e, ok);
-                lr[r] = wait_word(row + kHeadDim + 1, e, ok);
-                ar[r] = wait_word(row + dim, e, ok);
+                mr[r] = word_value(wm[r], row + kHeadDim, e, ok);
+                lr[r] = word_value(wl[r], row + kHeadDim + 1, e, ok);
+                ar[r] = word_value(wa[r], row + dim, e, ok);
             }
         }
         if (!ok) break;
