@@ -11,10 +11,13 @@
 //               issues the group's 4 Q rows and, per 88-key tile, one TMA tensor
 //               copy for K and one for V (22 KB each, one head, any K/V strides)
 //               into a 4-stage shared-memory ring, one mbarrier per stage and
-//               direction.
+//               direction.  The warp also writes each stage's Q rotated to the
+//               tile's first key position (RoPE is relative), so that the
+//               consumers rotate K by fixed per-lane factors only.
 //   warps 0..10 consumers: warp c owns keys [8c, 8c+8) of every tile, four at a
 //               time: 8 lanes per key, each lane 8 rotate_half pairs (16 of the
-//               128 dims).  Per key: RoPE of K (rope_unit.v), the 4 Q.K dot
+//               128 dims).  Per key: RoPE of K (rope_unit.v) relative to the
+//               tile's first key, the 4 Q.K dot
 //               products in FP32 (bf16_dot_product_mac.v + scale_unit.v), a
 //               3-level shuffle reduction, online softmax in log2 units
 //               (flash_softmax.v:233-490) and the P.V accumulation
@@ -51,8 +54,9 @@ namespace gqa {
 
 namespace {
 
-// 11 consumer warps + 1 producer warp = 12 warps: the most warps the 168
-// registers a consumer thread needs allow (64K registers per SM).
+// 11 consumer warps + 1 producer warp = 12 warps: the most warps the 160
+// registers a consumer thread needs allow (64K registers per SM; at 16 warps
+// the allocation would be 128).
 constexpr int kConsumerWarps = kDecodeConsumerWarps;
 constexpr int kKeysPerWarp = kDecodeKeysPerWarp;  // keys of one tile per warp
 constexpr int kTileKeys = kDecodeTileKeys;        // 88 keys per pipeline tile
@@ -63,7 +67,7 @@ constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kThreads = kConsumerThreads + 32;  // + the producer warp
 constexpr int kTileBytes = kTileKeys * kRowBytes;
 constexpr int kStageBytes = 2 * kTileBytes;
-constexpr int kReanchorTiles = 32;  // exact RoPE phase every 32 tiles (2048 keys)
+constexpr int kReanchorTiles = 32;  // exact RoPE phase every 32 tiles (2816 keys)
 // Epilogue: consumer thread tid owns outputs o = tid, tid + kConsumerThreads, ...
 // of the 4 x 128 (head, dim) outputs.
 constexpr int kOutputs = kGroup * kHeadDim;
@@ -74,12 +78,19 @@ constexpr int kOffQ = kOffBars + (2 * kStages + 2) * 8;  // the group's 4 Q rows
 constexpr int kOffP = kOffQ + kGroup * kRowBytes;
 constexpr int kPBytes = 2 * kConsumerWarps * kKeysPerWarp * kGroup * 8;  // [warp][2][key][head] (p, p)
 constexpr int kOffAlpha = kOffP + kPBytes;
-// Exact RoPE factors shared by the CTA's lanes (float2, kPairs per row): Q at
-// QUERY_POSITION and the CTA's first key.
-constexpr int kRopeQ = 0, kRopeBase = 1, kRopeRows = 2;
+// Exact RoPE factors of Q at QUERY_POSITION shared by the CTA's lanes (float2,
+// kPairs), for a pre-rotated K cache.
+constexpr int kRopeQ = 0, kRopeRows = 1;
 constexpr int kOffRope = kOffAlpha + 2 * kConsumerWarps * kGroup * 4;
 constexpr int kOffInfo = kOffRope + kRopeRows * kPairs * 8;
-constexpr int kSmemBytes = kOffInfo + 64;
+// Per stage, the group's Q rotated to the tile's first key and pre-scaled
+// (FP32, written by the producer warp): [head][re, im][half][g][4], so that
+// pair 8g + 4 half + e of a head's re (im) part sits at half*32 + 4g + e and a
+// consumer lane's two 16-byte loads per part are contiguous across g.
+constexpr int kQtFloats = kGroup * kHeadDim;
+constexpr int kOffQt = kOffInfo + 64;
+constexpr int kSmemBytes = kOffQt + kStages * kQtFloats * 4;
+static_assert(kOffQt % 16 == 0, "16-byte loads of the rotated Q");
 static_assert(kConsumerWarps * kGroup * kPartialFloats * 4 <= kOffBars, "warp merge buffer fits the ring");
 
 // Splits per sequence that split_merge_kernel merges in one pass.
@@ -97,18 +108,6 @@ __device__ __forceinline__ void cmul2(float2 ar, float2 ai, float2 br, float2 bi
     const float2 nbi = make_float2(-bi.x, -bi.y);
     cr = __ffma2_rn(ar, br, __fmul2_rn(ai, nbi));
     ci = __ffma2_rn(ar, bi, __fmul2_rn(ai, br));
-}
-
-// Exact factors of this lane's 8 pairs (8g .. 8g+7) at absolute position pos.
-__device__ __forceinline__ void rope_exact8(const RopeTable* rt, int g, int64_t pos, float2 (&wr)[4],
-                                            float2 (&wi)[4]) {
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-        const float2 f0 = rope_factor(rt->step[8 * g + 2 * jj], pos);
-        const float2 f1 = rope_factor(rt->step[8 * g + 2 * jj + 1], pos);
-        wr[jj] = make_float2(f0.x, f1.x);
-        wi[jj] = make_float2(f0.y, f1.y);
-    }
 }
 
 // The 8 factors of pairs 8g..8g+7 of one table row (shared or global memory).
@@ -162,25 +161,31 @@ __device__ __forceinline__ void write_result4(const OutSpec& o, int b, int qh, i
     }
 }
 
-// Producer (one thread): the group's Q rows, then per tile one TMA box for K
-// and one for V (88 rows of one head, whatever the K/V strides) into the
-// shared-memory ring; returns once its copies have landed.
+// RoPE constants the producer warp needs for pairs 2 lane and 2 lane + 1,
+// read from the immutable table before the grid dependency wait.
+struct ProducerRope {
+    uint64_t step0, step1;  // Q0.64 turns per position
+    float2 back_r, back_i;  // e^{-i theta kTileKeys}: one tile back
+};
+
+// Producer warp.  Lane 0 issues the group's 4 Q rows, then per tile one TMA
+// box for K and one for V (88 rows of one head, whatever the K/V strides) into
+// the shared-memory ring.  Unless K comes rotated, the whole warp also writes
+// each stage's Q: RoPE is relative, so with T the tile's first key position
+// and m the query position the score of key T + r is
+//   Re sum_i Q_T,i conj(k_i e^{i theta_i r}),  Q_T = q e^{i theta (m - T)} * qscale,
+// and the consumers rotate K by fixed per-lane factors e^{i theta r} only.  The
+// warp computes Q_T once per tile (2 pairs of 4 heads per lane: the factor
+// advances by one tile with a complex multiply, exactly every kReanchorTiles),
+// stores it and arrives on the stage's full barrier a second time.  Returns
+// once every copy into this CTA's shared memory has landed.
+template <bool kKRotated>
 __device__ __forceinline__ void produce_tiles(const DecodeArgs& a, uint8_t* smem, uint64_t* full, uint64_t* empty,
-                                             uint64_t* qbar, int b, int h, int hm, int64_t first_row, int n_tiles) {
+                                             uint64_t* qbar, int b, int h, int hm, int64_t first_row, int n_tiles,
+                                             int64_t q_minus_first, const ProducerRope& pr, int lane) {
     const uint64_t pol = l2_evict_first_policy();
-    // The group's Q rows go first, ahead of the K/V stream.
-    mbar_arrive_expect_tx(qbar, kGroup * kRowBytes);
-    for (int hq = 0; hq < kGroup; ++hq)
-        bulk_load(smem + kOffQ + hq * kRowBytes,
-                  a.q + (int64_t)b * a.q_bstride + (int64_t)(h * kGroup + hq) * a.q_hstride, kRowBytes, qbar, pol);
-    int issued = 0;
-    bool ok = true;
-    for (int t = 0; t < n_tiles; ++t) {
+    auto issue = [&](int t) {  // lane 0
         const int st = t % kStages;
-        if (t >= kStages && !mbar_wait(&empty[st], ((t / kStages) - 1) & 1)) {
-            ok = false;
-            break;
-        }
         uint8_t* kd = smem + st * kStageBytes;
         uint8_t* vd = kd + kTileBytes;
         mbar_arrive_expect_tx(&full[st], 2 * kTileBytes);
@@ -188,10 +193,88 @@ __device__ __forceinline__ void produce_tiles(const DecodeArgs& a, uint8_t* smem
         const int c1 = a.kv_rows_inner ? row : hm, c2 = a.kv_rows_inner ? hm : row;
         tma_load_3d(kd, &a.kmap, 0, c1, c2, &full[st], pol);
         tma_load_3d(vd, &a.vmap, 0, c1, c2, &full[st], pol);
-        issued = t + 1;
+    };
+    const int n_pre = min(n_tiles, kStages);
+    if (lane == 0) {
+        // The group's Q rows go first, ahead of the K/V stream; the first
+        // stages' copies need no wait.
+        mbar_arrive_expect_tx(qbar, kGroup * kRowBytes);
+        for (int hq = 0; hq < kGroup; ++hq)
+            bulk_load(smem + kOffQ + hq * kRowBytes,
+                      a.q + (int64_t)b * a.q_bstride + (int64_t)(h * kGroup + hq) * a.q_hstride, kRowBytes, qbar,
+                      pol);
+        for (int t = 0; t < n_pre; ++t) issue(t);
     }
+    int issued = n_pre, rotated = 0;  // tiles whose copies were issued / whose Q_T was written
+    bool ok = true;
+    if constexpr (!kKRotated) {
+        ok = mbar_wait(qbar, 0);
+        const uint8_t* qs = smem + kOffQ;
+        float2 q_re[kGroup], q_im[kGroup];  // pairs 2 lane, 2 lane + 1 of each head (BF16, exact)
+#pragma unroll
+        for (int hq = 0; hq < kGroup; ++hq) {
+            q_re[hq] = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(qs + hq * kRowBytes + 4 * lane));
+            q_im[hq] = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(qs + hq * kRowBytes + 128 + 4 * lane));
+        }
+        float2 gr, gi;  // qscale e^{i theta (m - T)} of the two pairs
+        auto exact = [&](int64_t pos) {
+            const float2 f0 = rope_factor(pr.step0, pos), f1 = rope_factor(pr.step1, pos);
+            gr = make_float2(f0.x * a.qscale, f1.x * a.qscale);
+            gi = make_float2(f0.y * a.qscale, f1.y * a.qscale);
+        };
+        exact(q_minus_first);
+        const int off = ((lane >> 1) & 1) * 32 + (lane >> 2) * 4 + 2 * (lane & 1);
+        float* qt_base = reinterpret_cast<float*>(smem + kOffQt);
+        for (int t = 0; t < n_tiles && ok; ++t) {
+            const int st = t % kStages;
+            if (t >= kStages) {
+                bool w = true;
+                if (lane == 0) {
+                    w = mbar_wait(&empty[st], ((t / kStages) - 1) & 1);
+                    if (w) issue(t);
+                }
+                if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
+                issued = t + 1;
+            }
+            float* qt = qt_base + st * kQtFloats;
+#pragma unroll
+            for (int hq = 0; hq < kGroup; ++hq) {
+                float2 re, im;
+                cmul2(q_re[hq], q_im[hq], gr, gi, re, im);
+                *reinterpret_cast<float2*>(qt + hq * kHeadDim + off) = re;
+                *reinterpret_cast<float2*>(qt + hq * kHeadDim + 64 + off) = im;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[st]);
+            rotated = t + 1;
+            if (((t + 1) % kReanchorTiles) == 0) {
+                exact(q_minus_first - (int64_t)(t + 1) * kTileKeys);
+            } else {
+                float2 nr, ni;
+                cmul2(gr, gi, pr.back_r, pr.back_i, nr, ni);
+                gr = nr;
+                gi = ni;
+            }
+        }
+    } else if (lane == 0) {
+        for (int t = kStages; t < n_tiles; ++t) {
+            if (!mbar_wait(&empty[t % kStages], ((t / kStages) - 1) & 1)) {
+                ok = false;
+                break;
+            }
+            issue(t);
+            issued = t + 1;
+        }
+    }
+    if (lane != 0) return;
     if (!ok) atomicOr(a.ws_status, kDevStatusTimeout);
-    // Do not leave while copies into this CTA's shared memory are in flight.
+    // Do not leave while copies into this CTA's shared memory are in flight
+    // (after a failed wait, complete the stages whose Q_T was not written).
+    if (!kKRotated)
+        for (int t = rotated; t < issued; ++t) mbar_arrive(&full[t % kStages]);
     mbar_wait(qbar, 0);
     for (int t = max(0, issued - kStages); t < issued; ++t) mbar_wait(&full[t % kStages], (t / kStages) & 1);
 }
@@ -481,7 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     // ---- set-up that reads only the argument block: before the dependency wait
     if (tid == kConsumerThreads) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], kKRotated ? 1 : 2);  // + the producer warp's Q_T
             mbar_init(&empty[s], kConsumerWarps);
         }
         mbar_init(qbar, 1);
@@ -489,20 +572,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         prefetch_tensormap(&a.kmap);
         prefetch_tensormap(&a.vmap);
     }
-    // Per-lane RoPE state: Q factors at QUERY_POSITION, the factors of this
-    // lane's key in step 0 of the first tile (first key x lane offset), and the
-    // fixed 4-key and one-tile advances.  Constant rows come from the immutable
-    // table (L2-resident after the first CTA); the two position-dependent rows
-    // are computed exactly, one factor per thread of the first 128.
-    float2 qfr[4], qfi[4], wr[4], wi[4], sr[4], si[4], tr[4], ti[4], lr[4], li[4];
+    // RoPE constants from the immutable table (L2-resident after the first
+    // CTA).  Unrotated K: each consumer lane's fixed factors e^{i theta r} of
+    // its key r of a tile in steps 0 and 1, and the producer warp's constants
+    // for Q_T.  Pre-rotated K: the consumers rotate Q once, at QUERY_POSITION
+    // (computed exactly, one factor per thread of the first 64).
+    float2 qfr[4], qfi[4], kfr[kSteps][4], kfi[kSteps][4];
+    ProducerRope prope{};
     if (!kKRotated && warp < kConsumerWarps) {
-        rope_row8(rt->rot_step, g, sr, si);
-        rope_row8(rt->rot_tile, g, tr, ti);
-        rope_row8(rt->lane_off[c * 4 + slot], g, lr, li);
+#pragma unroll
+        for (int step = 0; step < kSteps; ++step)
+            rope_row8(rt->key_off[c * kKeysPerWarp + step * 4 + slot], g, kfr[step], kfi[step]);
     }
-    auto lane_rope = [&](int qpos, int64_t first_pos) {
-        if (tid < 2 * kPairs)
-            rope[tid] = rope_factor(rt->step[tid & (kPairs - 1)], tid < kPairs ? (int64_t)qpos : first_pos);
+    if (!kKRotated && warp == kConsumerWarps) {
+        prope.step0 = rt->step[2 * lane];
+        prope.step1 = rt->step[2 * lane + 1];
+        const float2 t0 = rt->rot_tile[2 * lane], t1 = rt->rot_tile[2 * lane + 1];
+        prope.back_r = make_float2(t0.x, t1.x);
+        prope.back_i = make_float2(-t0.y, -t1.y);
+    }
+    auto lane_rope = [&](int qpos) {
+        if (tid < kPairs) rope[kRopeQ * kPairs + tid] = rope_factor(rt->step[tid], qpos);
         named_barrier_sync(1, kConsumerThreads);
         rope_row8(rope + kRopeQ * kPairs, g, qfr, qfi);
         if (a.flags & GQA_FLAG_Q_ROTATED) {  // Q supplied rotated: identity factors (exact)
@@ -512,14 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 qfi[jj] = make_float2(0.f, 0.f);
             }
         }
-        if (kKRotated) return;
-        float2 br[4], bi[4];
-        rope_row8(rope + kRopeBase * kPairs, g, br, bi);
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) cmul2(br[jj], bi[jj], lr[jj], li[jj], wr[jj], wi[jj]);
     };
-    if (single && warp < kConsumerWarps)
-        lane_rope(a.single.query_position, (int64_t)a.single.pos_begin + (int64_t)gsplit * a.chunk);
+    if (kKRotated && single && warp < kConsumerWarps) lane_rope(a.single.query_position);
     // A single sequence's split needs no memory read to know its keys: pull its
     // Q rows and first K/V tiles into L2 while the previous kernel in the stream
     // finishes (its loads below then hit L2).
@@ -625,7 +709,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     // In a cluster the whole warp also takes part in the epilogue's two cluster
     // barriers.
     if (warp == kConsumerWarps) {
-        if (lane == 0) produce_tiles(a, smem, full, empty, qbar, b, h, hm, first_row, n_tiles);
+        // m - T of the first tile (Q supplied rotated: m = 0).
+        const int64_t q_minus_first =
+            ((a.flags & GQA_FLAG_Q_ROTATED) ? 0 : (int64_t)d.query_position) - first_pos;
+        produce_tiles<kKRotated>(a, smem, full, empty, qbar, b, h, hm, first_row, n_tiles, q_minus_first, prope,
+                                 lane);
         if (clustered) {
             __syncwarp();
             cluster_sync_all();  // partials published
@@ -641,15 +729,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         for (int p = tid; p < n_pad; p += kConsumerThreads)
             a.mask_out[(int64_t)b * a.mask_stride + p] = key_valid(p, d.seq_len, qpos) ? 1 : 0;
     }
-    if (!single) lane_rope(qpos, first_pos);
+    if (kKRotated && !single) lane_rope(qpos);
 
-    // Q rotated at QUERY_POSITION and pre-scaled by scale*log2(e).  Register
-    // slot j of a lane holds Q head j ^ hh, so that the score reduction below
-    // needs no per-lane selects (each lane keeps slots 0/1 and sends 2/3).
+    // Q pre-scaled by scale*log2(e): rotated at QUERY_POSITION once (K
+    // pre-rotated), or to each tile's first key by the producer (loaded per
+    // tile in qk_tile).  Register slot j of a lane holds Q head j ^ hh, so
+    // that the score reduction below needs no per-lane selects (each lane
+    // keeps slots 0/1 and sends 2/3).
     float2 qr[kGroup][4], qi[kGroup][4];
-    bool ok = mbar_wait(qbar, 0);
+    bool ok = kKRotated ? mbar_wait(qbar, 0) : true;
 #pragma unroll
-    for (int j = 0; j < kGroup; ++j) {
+    for (int j = 0; j < kGroup && kKRotated; ++j) {
         const uint8_t* qrow = qs + (j ^ hh) * kRowBytes;
         const uint4 xr = *reinterpret_cast<const uint4*>(qrow + g * 16);
         const uint4 xi = *reinterpret_cast<const uint4*>(qrow + 128 + g * 16);
@@ -680,7 +770,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     auto qk_tile = [&](int t, float (&sc)[kSteps]) {
         const uint8_t* kt = smem + (t % kStages) * kStageBytes;
         const int rows = min(kTileKeys, cnt - t * kTileKeys);
-        float2 ur[4], ui[4];  // this lane's factors at step `step`: w * (e^{i theta 4})^step
+        if constexpr (!kKRotated) {
+            const float* qt = reinterpret_cast<const float*>(smem + kOffQt) + (t % kStages) * kQtFloats;
+#pragma unroll
+            for (int j = 0; j < kGroup; ++j) {
+                const float* row = qt + (j ^ hh) * kHeadDim + 4 * g;
+                const float4 r0 = *reinterpret_cast<const float4*>(row);
+                const float4 r1 = *reinterpret_cast<const float4*>(row + 32);
+                const float4 i0 = *reinterpret_cast<const float4*>(row + 64);
+                const float4 i1 = *reinterpret_cast<const float4*>(row + 96);
+                qr[j][0] = make_float2(r0.x, r0.y);
+                qr[j][1] = make_float2(r0.z, r0.w);
+                qr[j][2] = make_float2(r1.x, r1.y);
+                qr[j][3] = make_float2(r1.z, r1.w);
+                qi[j][0] = make_float2(i0.x, i0.y);
+                qi[j][1] = make_float2(i0.z, i0.w);
+                qi[j][2] = make_float2(i1.x, i1.y);
+                qi[j][3] = make_float2(i1.z, i1.w);
+            }
+        }
 #pragma unroll
         for (int step = 0; step < kSteps; ++step) {
             const int r = c * kKeysPerWarp + step * 4 + slot;
@@ -689,31 +797,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             const uint32_t xw[4] = {kre.x, kre.y, kre.z, kre.w};
             const uint32_t yw[4] = {kim.x, kim.y, kim.z, kim.w};
             float2 rr[4], ri[4];
-            if constexpr (kKRotated) {
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
+            for (int jj = 0; jj < 4; ++jj) {
+                if constexpr (kKRotated) {
                     rr[jj] = bf16x2_to_float2(xw[jj]);
                     ri[jj] = bf16x2_to_float2(yw[jj]);
+                } else {
+                    cmul2(bf16x2_to_float2(xw[jj]), bf16x2_to_float2(yw[jj]), kfr[step][jj], kfi[step][jj], rr[jj],
+                          ri[jj]);
                 }
-            } else {
-            if (step == 0) {
-#pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
-                    ur[jj] = wr[jj];
-                    ui[jj] = wi[jj];
-                }
-            } else {
-#pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
-                    float2 nr, ni;
-                    cmul2(ur[jj], ui[jj], sr[jj], si[jj], nr, ni);
-                    ur[jj] = nr;
-                    ui[jj] = ni;
-                }
-            }
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj)
-                cmul2(bf16x2_to_float2(xw[jj]), bf16x2_to_float2(yw[jj]), ur[jj], ui[jj], rr[jj], ri[jj]);
             }
             float s[kGroup];
 #pragma unroll
@@ -734,20 +826,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             float u = t0 + __shfl_xor_sync(0xffffffffu, t1, 2);
             u += __shfl_xor_sync(0xffffffffu, u, 1);
             sc[step] = r < rows ? u : -INFINITY;
-        }
-        // Advance the lane's RoPE factors by one tile (exactly every kReanchorTiles).
-        if (kKRotated) {
-            // no K factors
-        } else if (((t + 1) % kReanchorTiles) == 0) {
-            rope_exact8(rt, g, first_pos + (int64_t)(t + 1) * kTileKeys + c * kKeysPerWarp + slot, wr, wi);
-        } else {
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                float2 nr, ni;
-                cmul2(wr[jj], wi[jj], tr[jj], ti[jj], nr, ni);
-                wr[jj] = nr;
-                wi[jj] = ni;
-            }
         }
     };
 
@@ -1101,13 +1179,9 @@ void build_rope_table_host(double theta, RopeTable& t) {
     for (int i = 0; i < kPairs; ++i) {
         const double inv = std::pow(theta, -2.0 * i / (double)kHeadDim);
         t.step[i] = (uint64_t)std::llround(inv / two_pi * 18446744073709551616.0);  // < 2^62
-        t.rot_step[i] = make_float2((float)std::cos(4.0 * inv), (float)std::sin(4.0 * inv));
         t.rot_tile[i] = make_float2((float)std::cos(kTileKeys * inv), (float)std::sin(kTileKeys * inv));
-        for (int c = 0; c < kConsumerWarps; ++c)
-            for (int sl = 0; sl < 4; ++sl) {
-                const double ang = (double)(c * kKeysPerWarp + sl) * inv;
-                t.lane_off[c * 4 + sl][i] = make_float2((float)std::cos(ang), (float)std::sin(ang));
-            }
+        for (int r = 0; r < kTileKeys; ++r)
+            t.key_off[r][i] = make_float2((float)std::cos(r * inv), (float)std::sin(r * inv));
     }
 }
 }  // namespace

@@ -60,18 +60,13 @@ __host__ __device__ inline bool key_valid(int64_t p, int seq_len, int query_posi
 constexpr int kDecodeConsumerWarps = 11;
 constexpr int kDecodeKeysPerWarp = 8;
 constexpr int kDecodeTileKeys = kDecodeConsumerWarps * kDecodeKeysPerWarp;
-// Lane offsets: a consumer lane's first key sits (8c + s) keys after its CTA's
-// first key (warp c, slot s in 0..3).
-constexpr int kRopeLaneOffsets = kDecodeConsumerWarps * 4;
-
 // Immutable per-(device, rope_theta) RoPE table, computed on the host in double
 // precision and uploaded once.  Pair i turns theta^(-2i/128)/(2*pi) turns per
 // position; `step` holds that as an unsigned Q0.64 fraction.
 struct RopeTable {
     uint64_t step[kPairs];
-    float2 rot_step[kPairs];                  // e^{i theta_i * 4}: the second group of a warp's keys
     float2 rot_tile[kPairs];                  // e^{i theta_i * kDecodeTileKeys}: one tile further
-    float2 lane_off[kRopeLaneOffsets][kPairs];  // e^{i theta_i * (8c + s)}, row 4c + s
+    float2 key_off[kDecodeTileKeys][kPairs];  // e^{i theta_i * r}: key r of a tile relative to its first key
 };
 
 // Kernel argument block, passed by value as a __grid_constant__ parameter.  The
