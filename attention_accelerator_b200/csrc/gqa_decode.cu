@@ -22,7 +22,8 @@
 //               3-level shuffle reduction, online softmax in log2 units
 //               (flash_softmax.v:233-490) and the P.V accumulation
 //               (output_accumulator.v:244-536) with each lane owning 4 dims.
-//               The P.V of tile t-1 is interleaved with the Q.K of tile t.
+//               The Q.K and softmax of tile t and the P.V of tile t-1 form
+//               one branch-free block, so that they interleave.
 //   epilogue    the 11 warps' (m, l, acc) merge through shared memory; a sequence
 //               with one split writes its BF16 rows (O * 1/l,
 //               output_accumulator.v:546-687) directly.  Otherwise each split
@@ -829,8 +830,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         }
     };
 
-    // Online softmax of head hh over this warp's keys; publishes p and the rescale.
-    auto softmax_publish = [&](const float (&sc)[kSteps], int buf) {
+    // Online softmax of head hh over this warp's keys of one tile, in
+    // registers: the probabilities pv and the rescale alpha of the running sums.
+    auto softmax_tile = [&](const float (&sc)[kSteps], float (&pv)[kSteps], float& alpha) {
         float mx = sc[0];
 #pragma unroll
         for (int step = 1; step < kSteps; ++step) mx = fmaxf(mx, sc[step]);
@@ -838,9 +840,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
         const float m_new = fmaxf(m_run, mx);
         const float m_use = m_new == -INFINITY ? 0.f : m_new;
-        const float alpha = fast_exp2(m_run - m_use);
+        alpha = fast_exp2(m_run - m_use);
         float psum = 0.f;
-        float pv[kSteps];
 #pragma unroll
         for (int step = 0; step < kSteps; ++step) {
             pv[step] = fast_exp2(sc[step] - m_use);
@@ -848,25 +849,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         }
         l_run = l_run * alpha + psum;
         m_run = m_new;
+    };
+    // Stores p (as (p, p) pairs) and the rescale into the warp's buffer `buf`;
+    // the caller's __syncwarp publishes them to the warp.
+    auto publish = [&](const float (&pv)[kSteps], float alpha, int buf) {
         float2* pb = pw + buf * (kKeysPerWarp * kGroup);
         if ((g & 1) == 0) {
 #pragma unroll
             for (int step = 0; step < kSteps; ++step) pb[(step * 4 + slot) * kGroup + hh] = f2(pv[step]);
             if (slot == 0) aw[buf * kGroup + hh] = alpha;
         }
-        __syncwarp();
     };
 
     // acc = acc * alpha + sum_k p_k * V_k over this warp's keys of tile t.
-    auto pv_tile = [&](int t, int buf) {
+    // In the split's last tile, rows past its keys may hold anything (even
+    // NaN): their probabilities are 0, and each lane zeroes the 8 bytes of
+    // those rows that it reads itself, so no other lane is involved.
+    auto pv_tile = [&](int t, int buf, bool last) {
         uint8_t* vt = smem + (t % kStages) * kStageBytes + kTileBytes;
-        const int nr = min(kTileKeys, cnt - t * kTileKeys) - c * kKeysPerWarp;
-        if (nr < kKeysPerWarp) {
-            // Last tile of the split: rows past its keys may hold anything (even
-            // NaN).  Their probabilities are 0; zero their values too.
-            for (int rr = max(nr, 0); rr < kKeysPerWarp; ++rr)
-                *reinterpret_cast<uint2*>(vt + (c * kKeysPerWarp + rr) * kRowBytes + lane * 8) = make_uint2(0u, 0u);
-            __syncwarp();
+        if (last) {
+            const int nr = min(kTileKeys, cnt - t * kTileKeys) - c * kKeysPerWarp;
+#pragma unroll
+            for (int rr = 0; rr < kKeysPerWarp; ++rr)
+                if (rr >= nr)
+                    *reinterpret_cast<uint2*>(vt + (c * kKeysPerWarp + rr) * kRowBytes + lane * 8) = make_uint2(0u, 0u);
         }
         const float2* pb = pw + buf * (kKeysPerWarp * kGroup);
         const float4 al = *reinterpret_cast<const float4*>(aw + buf * kGroup);
@@ -892,13 +898,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         }
     };
 
-    // Software pipeline: the P.V of tile t-1 is issued in the same block as
-    // the Q.K of tile t, giving each warp two independent instruction streams.
+    // Software pipeline: one iteration computes the scores and the softmax of
+    // tile t and the P.V of tile t-1, with no branch or warp barrier between
+    // them, so that the two independent instruction streams interleave; the
+    // probabilities of tile t are stored after the P.V loads of tile t-1 (a
+    // different buffer) and published by one __syncwarp.
     if (ok && n_tiles > 0) {
         if (mbar_wait(&full[0], 0)) {
-            float sc[kSteps];
+            float sc[kSteps], pv[kSteps], alpha;
             qk_tile(0, sc);
-            softmax_publish(sc, 0);
+            softmax_tile(sc, pv, alpha);
+            publish(pv, alpha, 0);
+            __syncwarp();
         } else {
             ok = false;
         }
@@ -908,15 +919,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
             ok = false;
             break;
         }
-        float sc[kSteps];
+        float sc[kSteps], pv[kSteps], alpha;
         qk_tile(t, sc);
-        pv_tile(t - 1, (t - 1) & 1);
+        softmax_tile(sc, pv, alpha);
+        pv_tile(t - 1, (t - 1) & 1, false);
+        publish(pv, alpha, t & 1);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[(t - 1) % kStages]);
-        softmax_publish(sc, t & 1);
     }
     if (ok && n_tiles > 0) {
-        pv_tile(n_tiles - 1, (n_tiles - 1) & 1);
+        pv_tile(n_tiles - 1, (n_tiles - 1) & 1, true);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[(n_tiles - 1) % kStages]);
     }
