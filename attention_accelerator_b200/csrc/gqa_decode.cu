@@ -77,7 +77,7 @@ constexpr int kOutputs = kGroup * kHeadDim;
 constexpr int kOffBars = kStages * kStageBytes;       // full[kStages], empty[kStages], q
 constexpr int kOffQ = kOffBars + (2 * kStages + 2) * 8;  // the group's 4 Q rows (BF16)
 constexpr int kOffP = kOffQ + kGroup * kRowBytes;
-constexpr int kPBytes = 2 * kConsumerWarps * kKeysPerWarp * kGroup * 8;  // [warp][2][key][head] (p, p)
+constexpr int kPBytes = 2 * kConsumerWarps * kKeysPerWarp * kGroup * 4;  // [warp][2][key][head] p
 constexpr int kOffAlpha = kOffP + kPBytes;
 // Exact RoPE factors of Q at QUERY_POSITION shared by the CTA's lanes (float2,
 // kPairs), for a pre-rotated K cache.
@@ -109,6 +109,16 @@ __device__ __forceinline__ void cmul2(float2 ar, float2 ai, float2 br, float2 bi
     const float2 nbi = make_float2(-bi.x, -bi.y);
     cr = __ffma2_rn(ar, br, __fmul2_rn(ai, nbi));
     ci = __ffma2_rn(ar, bi, __fmul2_rn(ai, br));
+}
+
+// acc + (p, p) * v with p broadcast to both halves of the packed operand
+// (one 16-byte load then serves the 4 heads' probabilities of a key).
+__device__ __forceinline__ float2 ffma2_bcast(float p, float2 v, float2 acc) {
+    uint64_t r;
+    asm("{\n\t.reg .b64 pp;\n\tmov.b64 pp, {%1, %1};\n\tfma.rn.f32x2 %0, pp, %2, %3;\n\t}"
+        : "=l"(r)
+        : "f"(p), "l"(*reinterpret_cast<const uint64_t*>(&v)), "l"(*reinterpret_cast<const uint64_t*>(&acc)));
+    return *reinterpret_cast<const float2*>(&r);
 }
 
 // The 8 factors of pairs 8g..8g+7 of one table row (shared or global memory).
@@ -538,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
     uint64_t* empty = full + kStages;
-    float2* pbuf = reinterpret_cast<float2*>(smem + kOffP);
+    float* pbuf = reinterpret_cast<float*>(smem + kOffP);
     float* abuf = reinterpret_cast<float*>(smem + kOffAlpha);
     float2* rope = reinterpret_cast<float2*>(smem + kOffRope);
     int* info = reinterpret_cast<int*>(smem + kOffInfo);
@@ -760,8 +770,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     float2 acc0[kGroup], acc1[kGroup];  // dims (4*lane, +1) and (4*lane+2, +3) of each head
 #pragma unroll
     for (int hq = 0; hq < kGroup; ++hq) acc0[hq] = acc1[hq] = make_float2(0.f, 0.f);
-    // Per-warp double buffer of probabilities [2][keys][4 heads] as (p, p) pairs, and rescales [2][4].
-    float2* pw = pbuf + c * 2 * (kKeysPerWarp * kGroup);
+    // Per-warp double buffer of probabilities [2][keys][4 heads] and rescales [2][4].
+    float* pw = pbuf + c * 2 * (kKeysPerWarp * kGroup);
     float* aw = abuf + c * 2 * kGroup;
 
     // Scores of this warp's keys of tile t: RoPE of K, Q.K for the 4 heads,
@@ -850,13 +860,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         l_run = l_run * alpha + psum;
         m_run = m_new;
     };
-    // Stores p (as (p, p) pairs) and the rescale into the warp's buffer `buf`;
-    // the caller's __syncwarp publishes them to the warp.
+    // Stores p and the rescale into the warp's buffer `buf`; the caller's
+    // __syncwarp publishes them to the warp.
     auto publish = [&](const float (&pv)[kSteps], float alpha, int buf) {
-        float2* pb = pw + buf * (kKeysPerWarp * kGroup);
+        float* pb = pw + buf * (kKeysPerWarp * kGroup);
         if ((g & 1) == 0) {
 #pragma unroll
-            for (int step = 0; step < kSteps; ++step) pb[(step * 4 + slot) * kGroup + hh] = f2(pv[step]);
+            for (int step = 0; step < kSteps; ++step) pb[(step * 4 + slot) * kGroup + hh] = pv[step];
             if (slot == 0) aw[buf * kGroup + hh] = alpha;
         }
     };
@@ -874,7 +884,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
                 if (rr >= nr)
                     *reinterpret_cast<uint2*>(vt + (c * kKeysPerWarp + rr) * kRowBytes + lane * 8) = make_uint2(0u, 0u);
         }
-        const float2* pb = pw + buf * (kKeysPerWarp * kGroup);
+        const float* pb = pw + buf * (kKeysPerWarp * kGroup);
         const float4 al = *reinterpret_cast<const float4*>(aw + buf * kGroup);
         const float alv[4] = {al.x, al.y, al.z, al.w};
 #pragma unroll
@@ -884,16 +894,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         }
 #pragma unroll
         for (int rr = 0; rr < kKeysPerWarp; ++rr) {
-            const float4 p01 = *reinterpret_cast<const float4*>(pb + rr * kGroup);
-            const float4 p23 = *reinterpret_cast<const float4*>(pb + rr * kGroup + 2);
+            const float4 p4 = *reinterpret_cast<const float4*>(pb + rr * kGroup);
             const uint2 vv = *reinterpret_cast<const uint2*>(vt + (c * kKeysPerWarp + rr) * kRowBytes + lane * 8);
             const float2 v0 = bf16x2_to_float2(vv.x), v1 = bf16x2_to_float2(vv.y);
-            const float2 pk[4] = {make_float2(p01.x, p01.y), make_float2(p01.z, p01.w), make_float2(p23.x, p23.y),
-                                  make_float2(p23.z, p23.w)};
+            const float pk[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
             for (int hq = 0; hq < kGroup; ++hq) {
-                acc0[hq] = __ffma2_rn(pk[hq], v0, acc0[hq]);
-                acc1[hq] = __ffma2_rn(pk[hq], v1, acc1[hq]);
+                acc0[hq] = ffma2_bcast(pk[hq], v0, acc0[hq]);
+                acc1[hq] = ffma2_bcast(pk[hq], v1, acc1[hq]);
             }
         }
     };
