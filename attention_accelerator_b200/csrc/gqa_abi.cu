@@ -40,8 +40,9 @@ int check_device_memory(std::initializer_list<const void*> ptrs) {
 namespace {
 
 constexpr int kMaxDevices = 64;
-constexpr size_t kWsHeaderBytes = 256;  // status word at 0, per-KV-head arrival counters at 64
+constexpr size_t kWsHeaderBytes = 256;  // status word at 0, per-KV-head arrival counters at 64, work queue at 128
 constexpr size_t kWsArrivalsOffset = 64;
+constexpr size_t kWsWorkOffset = 128;  // a batch's work queue: next item, CTAs done
 constexpr int kMinChunk = gqa::kDecodeTileKeys;  // keys: one pipeline tile
 constexpr int kMinChunkMultiWave = 256;
 constexpr int kMaxWaves = 16;
@@ -634,6 +635,10 @@ int gqa_decode_batched(const void* q, const void* k, const void* v, void* out, c
     if (st != GQA_OK) return st;
     a.descs = batch == 1 ? nullptr : reinterpret_cast<const gqa::SeqDesc*>(dev_descs);
     a.single = d[0];
+    if (batch > 1) {  // decode_queue_kernel: one CTA per SM works through the (split, KV head) items
+        a.ws_work = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + kWsWorkOffset);
+        a.n_items = pl.total_splits * a.n_heads;
+    }
     if (batch == 1) {
         a.cluster = pl.cluster;
         if (pl.cluster == 0 && pl.total_splits > 1 && pl.total_splits <= gqa::decode_last_merge_max_splits())

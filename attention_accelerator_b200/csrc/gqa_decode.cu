@@ -48,6 +48,7 @@
 #include "gqa_device.cuh"
 #include "gqa_internal.h"
 
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 
@@ -288,6 +289,115 @@ __device__ __forceinline__ void produce_tiles(const DecodeArgs& a, uint8_t* smem
         for (int t = rotated; t < issued; ++t) mbar_arrive(&full[t % kStages]);
     mbar_wait(qbar, 0);
     for (int t = max(0, issued - kStages); t < issued; ++t) mbar_wait(&full[t % kStages], (t / kStages) & 1);
+}
+
+// ---------------------------------------------------------------------------
+// decode_queue_kernel (a batch): its shared memory is decode_kernel's ring, P,
+// alpha, RoPE and Q_T regions at the same offsets, and behind them
+//   barriers  full/empty are decode_kernel's; here qbar[2] (two Q-row slots),
+//             filled[2] and freed[2] (two item slots: the producer warp fills
+//             one, the consumer warps free it once read)
+//   Q rows    [2 slots][4 rows] BF16
+//   items     [2 slots][kItemInts] ints
+//   epilogue  the warps' partials and factors, outside the ring so that the
+//             next item's tiles can land while it is in use.
+// ---------------------------------------------------------------------------
+constexpr int kItemInts = 16;
+constexpr int kQueueOffBars = kSmemBytes;
+constexpr int kQueueOffQ = kQueueOffBars + 6 * 8;
+constexpr int kQueueOffItems = kQueueOffQ + 2 * kGroup * kRowBytes;
+constexpr int kQueueOffEpi = kQueueOffItems + 2 * kItemInts * 4;
+constexpr int kQueueEpiFloats = kConsumerWarps * kGroup * kPartialFloats + 2 * kConsumerWarps * kGroup + kGroup;
+constexpr int kQueueSmemBytes = kQueueOffEpi + kQueueEpiFloats * 4;
+static_assert(kQueueOffQ % 16 == 0 && kQueueOffEpi % 16 == 0, "16-byte aligned regions");
+static_assert(kQueueSmemBytes <= 227 * 1024, "shared memory of one CTA");
+
+// Producer warp of decode_queue_kernel, one item (a split of one KV head).
+// Lane 0 issues the group's 4 Q rows into the slot `qrows` (barrier qbar),
+// then per tile one TMA box for K and one for V into ring positions ring0,
+// ring0 + 1, ... (stage p % kStages), first waiting for the stage's release
+// once the ring has gone round.  Unless K comes rotated the warp also writes
+// each stage's Q_T and arrives on its full barrier a second time, as
+// produce_tiles does.  `issued` and `rotated` end as one past the last ring
+// position whose copies were issued and whose Q_T was written; false after a
+// timed-out wait.
+template <bool kKRotated>
+__device__ __forceinline__ bool produce_item(const DecodeArgs& a, uint8_t* smem, uint64_t* full, uint64_t* empty,
+                                             uint64_t* qbar, uint32_t qparity, uint8_t* qrows, int b, int h, int hm,
+                                             int64_t first_row, int n_tiles, int64_t q_minus_first,
+                                             const ProducerRope& pr, int lane, int ring0, int& issued, int& rotated) {
+    const uint64_t pol = l2_evict_first_policy();
+    if (lane == 0) {
+        // The group's Q rows go first, ahead of the item's K/V stream.
+        mbar_arrive_expect_tx(qbar, kGroup * kRowBytes);
+        for (int hq = 0; hq < kGroup; ++hq)
+            bulk_load(qrows + hq * kRowBytes,
+                      a.q + (int64_t)b * a.q_bstride + (int64_t)(h * kGroup + hq) * a.q_hstride, kRowBytes, qbar,
+                      pol);
+    }
+    float2 q_re[kGroup], q_im[kGroup];  // pairs 2 lane, 2 lane + 1 of each head (BF16, exact)
+    float2 gr, gi;                      // qscale e^{i theta (m - T)} of the two pairs
+    auto exact = [&](int64_t pos) {
+        const float2 f0 = rope_factor(pr.step0, pos), f1 = rope_factor(pr.step1, pos);
+        gr = make_float2(f0.x * a.qscale, f1.x * a.qscale);
+        gi = make_float2(f0.y * a.qscale, f1.y * a.qscale);
+    };
+    if (!kKRotated) exact(q_minus_first);
+    const int off = ((lane >> 1) & 1) * 32 + (lane >> 2) * 4 + 2 * (lane & 1);
+    float* qt_base = reinterpret_cast<float*>(smem + kOffQt);
+    for (int t = 0; t < n_tiles; ++t) {
+        const int p = ring0 + t, st = p % kStages;
+        bool w = true;
+        if (lane == 0) {
+            if (p >= kStages) w = mbar_wait(&empty[st], ((p / kStages) - 1) & 1);
+            if (w) {
+                uint8_t* kd = smem + st * kStageBytes;
+                uint8_t* vd = kd + kTileBytes;
+                mbar_arrive_expect_tx(&full[st], 2 * kTileBytes);
+                const int row = static_cast<int>(first_row + (int64_t)t * kTileKeys);
+                const int c1 = a.kv_rows_inner ? row : hm, c2 = a.kv_rows_inner ? hm : row;
+                tma_load_3d(kd, &a.kmap, 0, c1, c2, &full[st], pol);
+                tma_load_3d(vd, &a.vmap, 0, c1, c2, &full[st], pol);
+            }
+        }
+        if (!__shfl_sync(0xffffffffu, w ? 1 : 0, 0)) return false;
+        issued = p + 1;
+        if constexpr (!kKRotated) {
+            if (t == 0) {  // the tile's copies are on their way: now wait for the Q rows
+                const bool okq = mbar_wait(qbar, qparity);
+                if (!__all_sync(0xffffffffu, okq)) return false;
+#pragma unroll
+                for (int hq = 0; hq < kGroup; ++hq) {
+                    q_re[hq] = bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(qrows + hq * kRowBytes + 4 * lane));
+                    q_im[hq] =
+                        bf16x2_to_float2(*reinterpret_cast<const uint32_t*>(qrows + hq * kRowBytes + 128 + 4 * lane));
+                }
+            }
+            float* qt = qt_base + st * kQtFloats;
+#pragma unroll
+            for (int hq = 0; hq < kGroup; ++hq) {
+                float2 re, im;
+                cmul2(q_re[hq], q_im[hq], gr, gi, re, im);
+                *reinterpret_cast<float2*>(qt + hq * kHeadDim + off) = re;
+                *reinterpret_cast<float2*>(qt + hq * kHeadDim + 64 + off) = im;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[st]);
+            rotated = p + 1;
+            if (((t + 1) % kReanchorTiles) == 0) {
+                exact(q_minus_first - (int64_t)(t + 1) * kTileKeys);
+            } else {
+                float2 nr, ni;
+                cmul2(gr, gi, pr.back_r, pr.back_i, nr, ni);
+                gr = nr;
+                gi = ni;
+            }
+        }
+    }
+    // An item without keys: its Q-row copy must still complete before the
+    // slot is used again.
+    if (!kKRotated && n_tiles == 0 && !__all_sync(0xffffffffu, mbar_wait(qbar, qparity))) return false;
+    return true;
 }
 
 // Cluster epilogue of a single sequence: the n splits (CTA ranks 0..n-1) of KV
@@ -1022,6 +1132,512 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
 }
 
 // ---------------------------------------------------------------------------
+// decode_queue_kernel: the decode of a batch of sequences, one CTA per SM.
+// Each CTA's producer warp takes items w = 0, 1, ... in order from a work
+// queue in the workspace header, item w being split w / n_heads of the plan,
+// of KV head w % n_heads: decode_kernel's CTA order, every sequence's
+// full-chunk splits first and the shorter last splits after them.  The
+// consumers compute each item exactly as decode_kernel does and store its FP32
+// partial (a sequence of one split: its BF16 rows); split_merge_kernel then
+// finishes the sequences.  The next item's Q rows and tiles stream into the
+// ring while the consumers merge the current one, so an SM does not sit idle
+// between splits as it does between the CTAs of a grid of one split per CTA.
+// Which CTA computes an item does not change its result.
+// ---------------------------------------------------------------------------
+template <bool kKRotated>
+__global__ void __launch_bounds__(kThreads, 1) decode_queue_kernel(const __grid_constant__ DecodeArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
+    uint64_t* empty = full + kStages;
+    uint64_t* qbar = reinterpret_cast<uint64_t*>(smem + kQueueOffBars);  // [2]: the Q-row slots
+    uint64_t* slot_filled = qbar + 2;                                       // [2]: an item slot written
+    uint64_t* slot_freed = qbar + 4;                                        // [2]: an item slot read
+    int* slots = reinterpret_cast<int*>(smem + kQueueOffItems);            // [2][kItemInts]
+    float* pbuf = reinterpret_cast<float*>(smem + kOffP);
+    float* abuf = reinterpret_cast<float*>(smem + kOffAlpha);
+    float2* rope = reinterpret_cast<float2*>(smem + kOffRope);
+    const RopeTable* rt = a.rope;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int tid = threadIdx.x;
+    const int c = warp;
+    const int slot = lane >> 3;  // key within the group of 4 a step handles
+    const int g = lane & 7;      // pairs 8g .. 8g+7 (dims 8g..8g+7 and 64+8g..64+8g+7)
+    const int hh = g >> 1;       // Q head whose score this lane holds after the reduction
+
+    // ---- set-up that reads only the argument block: before the dependency wait
+    if (tid == kConsumerThreads) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], kKRotated ? 1 : 2);  // + the producer warp's Q_T
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&qbar[s], 1);
+            mbar_init(&slot_filled[s], 1);
+            mbar_init(&slot_freed[s], kConsumerWarps);  // one arrival per consumer warp
+        }
+        fence_barrier_init();
+        prefetch_tensormap(&a.kmap);
+        prefetch_tensormap(&a.vmap);
+    }
+    // RoPE constants, as in decode_kernel.
+    float2 qfr[4], qfi[4], kfr[kSteps][4], kfi[kSteps][4];
+    ProducerRope prope{};
+    if (!kKRotated && warp < kConsumerWarps) {
+#pragma unroll
+        for (int step = 0; step < kSteps; ++step)
+            rope_row8(rt->key_off[c * kKeysPerWarp + step * 4 + slot], g, kfr[step], kfi[step]);
+    }
+    if (!kKRotated && warp == kConsumerWarps) {
+        prope.step0 = rt->step[2 * lane];
+        prope.step1 = rt->step[2 * lane + 1];
+        const float2 t0 = rt->rot_tile[2 * lane], t1 = rt->rot_tile[2 * lane + 1];
+        prope.back_r = make_float2(t0.x, t1.x);
+        prope.back_i = make_float2(-t0.y, -t1.y);
+    }
+    auto lane_rope = [&](int qpos) {
+        if (tid < kPairs) rope[kRopeQ * kPairs + tid] = rope_factor(rt->step[tid], qpos);
+        named_barrier_sync(1, kConsumerThreads);
+        rope_row8(rope + kRopeQ * kPairs, g, qfr, qfi);
+        if (a.flags & GQA_FLAG_Q_ROTATED) {  // Q supplied rotated: identity factors (exact)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                qfr[jj] = make_float2(1.f, 1.f);
+                qfi[jj] = make_float2(0.f, 0.f);
+            }
+        }
+    };
+    __syncthreads();  // the barriers are initialised
+    allow_dependent_launch();
+    grid_dependency_wait();
+
+    // ======================= producer warp =======================
+    if (warp == kConsumerWarps) {
+        int ring = 0, issued = 0, rotated = 0, n_q = 0;
+        bool ok = true;
+        for (int k = 0; ok; ++k) {
+            const int sl = k & 1;
+            int w = 0;
+            if (lane == 0) w = (int)atomicAdd(a.ws_work, 1u);
+            w = __shfl_sync(0xffffffffu, w, 0);
+            bool valid = w < a.n_items;
+            const int item_split = w / a.n_heads, item_hm = w % a.n_heads;
+            // The slot (and its Q rows) of item k - 2 must have been read.
+            if (k >= 2) {
+                bool w2 = true;
+                if (lane == 0) w2 = mbar_wait(&slot_freed[sl], ((k >> 1) - 1) & 1);
+                if (!__shfl_sync(0xffffffffu, w2 ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
+            }
+            int b = 0, split = item_split, logical = item_split;
+            if (valid) {
+                // Sequence b has full_b = keys / chunk full splits and
+                // seq_splits - full_b (0 or 1) shorter last ones.
+                auto counts = [&](int bb, int& nf, int& np) {
+                    nf = np = 0;
+                    if (bb < a.batch) {
+                        const SeqDesc db = a.descs[bb];
+                        nf = seq_key_count(db) / a.chunk;
+                        np = seq_splits(db, a.chunk) - nf;
+                    }
+                };
+                auto scan = [&](int v) {
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const int t = __shfl_up_sync(0xffffffffu, v, o);
+                        if (lane >= o) v += t;
+                    }
+                    return v;
+                };
+                int total_full = 0;
+                for (int b0 = 0; b0 < a.batch; b0 += 32) {
+                    int nf, np;
+                    counts(b0 + lane, nf, np);
+                    total_full += __shfl_sync(0xffffffffu, scan(nf), 31);
+                }
+                const bool in_full = item_split < total_full;
+                const int target = in_full ? item_split : item_split - total_full;
+                int base = 0, sbase = 0;  // splits of the chosen kind / of any kind before b0
+                b = -1;
+                for (int b0 = 0; b0 < a.batch && b < 0; b0 += 32) {
+                    int nf, np;
+                    counts(b0 + lane, nf, np);
+                    const int nk = in_full ? nf : np;
+                    const int incl = scan(nk), sincl = scan(nf + np);
+                    const int excl = incl - nk;
+                    const bool hit = b0 + lane < a.batch && target >= base + excl && target < base + incl;
+                    const unsigned m = __ballot_sync(0xffffffffu, hit);
+                    if (m) {
+                        const int src = __ffs(m) - 1;
+                        b = b0 + src;
+                        const int nf_src = __shfl_sync(0xffffffffu, nf, src);
+                        split = in_full ? target - base - __shfl_sync(0xffffffffu, excl, src) : nf_src;
+                        const int sexcl = __shfl_sync(0xffffffffu, sincl - (nf + np), src);
+                        logical = sbase + sexcl + split;
+                    }
+                    base += __shfl_sync(0xffffffffu, incl, 31);
+                    sbase += __shfl_sync(0xffffffffu, sincl, 31);
+                }
+                valid = b >= 0;
+            }
+            SeqDesc d = a.single;
+            if (valid) d = a.descs[b];
+            const int key0 = split * a.chunk;
+            const int cnt = max(0, min(a.chunk, seq_key_count(d) - key0));
+            if (lane == 0) {  // everything the consumers need to know about the item
+                int* it = slots + sl * kItemInts;
+                it[0] = valid ? 1 : 0;
+                it[1] = b;
+                it[2] = split;
+                it[3] = logical;
+                it[4] = item_hm;
+                it[5] = seq_splits(d, a.chunk);
+                it[6] = cnt;
+                it[7] = d.query_position;
+                it[8] = d.seq_len;
+                mbar_arrive(&slot_filled[sl]);
+            }
+            if (!valid) break;
+            const int n_tiles = (cnt + kTileKeys - 1) / kTileKeys;
+            // m - T of the item's first tile (Q supplied rotated: m = 0).
+            const int64_t q_minus_first =
+                ((a.flags & GQA_FLAG_Q_ROTATED) ? 0 : (int64_t)d.query_position) - ((int64_t)d.pos_begin + key0);
+            ok = produce_item<kKRotated>(a, smem, full, empty, &qbar[sl], (uint32_t)((k >> 1) & 1),
+                                         smem + kQueueOffQ + sl * kGroup * kRowBytes, b, a.head0 + item_hm,
+                                         item_hm, d.kv_start + key0, n_tiles, q_minus_first, prope, lane, ring,
+                                         issued, rotated);
+            n_q = k + 1;
+            ring += n_tiles;
+        }
+        if (lane == 0) {
+            if (!ok) atomicOr(a.ws_status, kDevStatusTimeout);
+            // Do not leave while copies into this CTA's shared memory are in
+            // flight (after a failed wait, complete the stages whose Q_T was
+            // not written).
+            if (!kKRotated)
+                for (int p = rotated; p < issued; ++p) mbar_arrive(&full[p % kStages]);
+            for (int p = max(0, issued - kStages); p < issued; ++p) mbar_wait(&full[p % kStages], (p / kStages) & 1);
+            for (int k = max(0, n_q - 2); k < n_q; ++k) mbar_wait(&qbar[k & 1], (k >> 1) & 1);
+            // The last CTA to leave the queue clears it for the next call (which
+            // starts after this grid completes).
+            if (arrive_acq_rel_gpu(a.ws_work + 1) == gridDim.x - 1) {
+                a.ws_work[0] = 0u;
+                a.ws_work[1] = 0u;
+            }
+        }
+        return;
+    }
+
+    // ======================= consumer warps =======================
+    float* pw = pbuf + c * 2 * (kKeysPerWarp * kGroup);  // this warp's probabilities [2][keys][4 heads]
+    float* aw = abuf + c * 2 * kGroup;                    // and rescales [2][4]
+    float* cb = reinterpret_cast<float*>(smem + kQueueOffEpi);
+    float* wf = cb + kConsumerWarps * kGroup * kPartialFloats;  // [w][hq]  2^(m_w - M)
+    float* wl = wf + kConsumerWarps * kGroup;                   // [w][hq]  l_w * 2^(m_w - M)
+    float* wm = wl + kConsumerWarps * kGroup;                   // [hq]     M
+    const OutSpec direct{a.out, a.o_bstride, a.o_hstride, a.flags};
+    bool ok = true;
+    int ring0 = 0;  // ring position of the item's first tile
+    for (int k = 0;; ++k) {
+        const int sl = k & 1;
+        // Every consumer warp runs the same items: a wait that timed out in one
+        // of them stops all of them here (named barriers do not time out).
+        const bool filled = mbar_wait(&slot_filled[sl], (k >> 1) & 1);
+        if (named_barrier_or(1, kConsumerThreads, !filled)) {
+            ok = false;
+            break;
+        }
+        const int* it = slots + sl * kItemInts;
+        if (it[0] == 0) break;
+        const int b = it[1];
+        const int split = it[2];
+        const int lsplit = it[3];  // storage index of this split's partial
+        const int hm = it[4];
+        const int h = a.head0 + hm;
+        const int n_split = it[5];
+        const int cnt = it[6];
+        const int qpos = it[7];
+        const int seq_len = it[8];
+        const int n_tiles = (cnt + kTileKeys - 1) / kTileKeys;
+
+        // Q pre-scaled by scale*log2(e): rotated at QUERY_POSITION once per item
+        // (K pre-rotated), or to each tile's first key by the producer (loaded
+        // per tile in qk_tile).  Register slot j of a lane holds Q head j ^ hh.
+        float2 qr[kGroup][4], qi[kGroup][4];
+        if constexpr (kKRotated) {
+            lane_rope(qpos);
+            ok = mbar_wait(&qbar[sl], (k >> 1) & 1);
+            const uint8_t* qs = smem + kQueueOffQ + sl * kGroup * kRowBytes;
+#pragma unroll
+            for (int j = 0; j < kGroup; ++j) {
+                const uint8_t* qrow = qs + (j ^ hh) * kRowBytes;
+                const uint4 xr = *reinterpret_cast<const uint4*>(qrow + g * 16);
+                const uint4 xi = *reinterpret_cast<const uint4*>(qrow + 128 + g * 16);
+                const uint32_t xw[4] = {xr.x, xr.y, xr.z, xr.w};
+                const uint32_t yw[4] = {xi.x, xi.y, xi.z, xi.w};
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    float2 re, im;
+                    cmul2(bf16x2_to_float2(xw[jj]), bf16x2_to_float2(yw[jj]), qfr[jj], qfi[jj], re, im);
+                    qr[j][jj] = __fmul2_rn(re, f2(a.qscale));
+                    qi[j][jj] = __fmul2_rn(im, f2(a.qscale));
+                }
+            }
+        }
+        // The slot (and its Q rows) may be reused.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&slot_freed[sl]);
+
+        // The split merge finds each sequence's splits here.
+        if (split == 0 && hm == 0 && tid == 0 && n_split > 1) a.ws_seqinfo[b] = make_int2(lsplit, n_split);
+        if (a.mask_out != nullptr && split == 0 && hm == 0) {
+            const int n_pad = ((seq_len + a.kv_block_len - 1) / a.kv_block_len) * a.kv_block_len;
+            for (int p = tid; p < n_pad; p += kConsumerThreads)
+                a.mask_out[(int64_t)b * a.mask_stride + p] = key_valid(p, seq_len, qpos) ? 1 : 0;
+        }
+
+        float m_run = -INFINITY;  // running max (log2 units) of head hh
+        float l_run = 0.f;        // running sum of this lane's key slot for head hh
+        float2 acc0[kGroup], acc1[kGroup];  // dims (4*lane, +1) and (4*lane+2, +3) of each head
+#pragma unroll
+        for (int hq = 0; hq < kGroup; ++hq) acc0[hq] = acc1[hq] = make_float2(0.f, 0.f);
+
+        // Scores of this warp's keys of tile t: RoPE of K, Q.K for the 4 heads,
+        // reduction over the 8 lanes of each key.  Keys [key0, key0 + cnt) all
+        // satisfy key_valid() (they lie in [0, min(SEQ_LEN, QUERY_POSITION + 1)));
+        // rows past them are masked.
+        auto qk_tile = [&](int t, float (&sc)[kSteps]) {
+            const uint8_t* kt = smem + ((ring0 + t) % kStages) * kStageBytes;
+            const int rows = min(kTileKeys, cnt - t * kTileKeys);
+            if constexpr (!kKRotated) {
+                const float* qt = reinterpret_cast<const float*>(smem + kOffQt) + ((ring0 + t) % kStages) * kQtFloats;
+#pragma unroll
+                for (int j = 0; j < kGroup; ++j) {
+                    const float* row = qt + (j ^ hh) * kHeadDim + 4 * g;
+                    const float4 r0 = *reinterpret_cast<const float4*>(row);
+                    const float4 r1 = *reinterpret_cast<const float4*>(row + 32);
+                    const float4 i0 = *reinterpret_cast<const float4*>(row + 64);
+                    const float4 i1 = *reinterpret_cast<const float4*>(row + 96);
+                    qr[j][0] = make_float2(r0.x, r0.y);
+                    qr[j][1] = make_float2(r0.z, r0.w);
+                    qr[j][2] = make_float2(r1.x, r1.y);
+                    qr[j][3] = make_float2(r1.z, r1.w);
+                    qi[j][0] = make_float2(i0.x, i0.y);
+                    qi[j][1] = make_float2(i0.z, i0.w);
+                    qi[j][2] = make_float2(i1.x, i1.y);
+                    qi[j][3] = make_float2(i1.z, i1.w);
+                }
+            }
+#pragma unroll
+            for (int step = 0; step < kSteps; ++step) {
+                const int r = c * kKeysPerWarp + step * 4 + slot;
+                const uint4 kre = *reinterpret_cast<const uint4*>(kt + r * kRowBytes + g * 16);
+                const uint4 kim = *reinterpret_cast<const uint4*>(kt + r * kRowBytes + 128 + g * 16);
+                const uint32_t xw[4] = {kre.x, kre.y, kre.z, kre.w};
+                const uint32_t yw[4] = {kim.x, kim.y, kim.z, kim.w};
+                float2 rr[4], ri[4];
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    if constexpr (kKRotated) {
+                        rr[jj] = bf16x2_to_float2(xw[jj]);
+                        ri[jj] = bf16x2_to_float2(yw[jj]);
+                    } else {
+                        cmul2(bf16x2_to_float2(xw[jj]), bf16x2_to_float2(yw[jj]), kfr[step][jj], kfi[step][jj], rr[jj],
+                              ri[jj]);
+                    }
+                }
+                float s[kGroup];
+#pragma unroll
+                for (int hq = 0; hq < kGroup; ++hq) {
+                    float2 acc = __fmul2_rn(qr[hq][0], rr[0]);
+                    acc = __ffma2_rn(qi[hq][0], ri[0], acc);
+#pragma unroll
+                    for (int jj = 1; jj < 4; ++jj) {
+                        acc = __ffma2_rn(qr[hq][jj], rr[jj], acc);
+                        acc = __ffma2_rn(qi[hq][jj], ri[jj], acc);
+                    }
+                    s[hq] = acc.x + acc.y;
+                }
+                // Lanes l and l^4 hold the same heads in swapped slot pairs, lanes l
+                // and l^2 in swapped slots: keep 0/1, send 2/3; keep 0, send 1.
+                const float t0 = s[0] + __shfl_xor_sync(0xffffffffu, s[2], 4);
+                const float t1 = s[1] + __shfl_xor_sync(0xffffffffu, s[3], 4);
+                float u = t0 + __shfl_xor_sync(0xffffffffu, t1, 2);
+                u += __shfl_xor_sync(0xffffffffu, u, 1);
+                sc[step] = r < rows ? u : -INFINITY;
+            }
+        };
+
+        // Online softmax of head hh over this warp's keys of one tile, in
+        // registers: the probabilities pv and the rescale alpha of the running sums.
+        auto softmax_tile = [&](const float (&sc)[kSteps], float (&pv)[kSteps], float& alpha) {
+            float mx = sc[0];
+#pragma unroll
+            for (int step = 1; step < kSteps; ++step) mx = fmaxf(mx, sc[step]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float m_new = fmaxf(m_run, mx);
+            const float m_use = m_new == -INFINITY ? 0.f : m_new;
+            alpha = fast_exp2(m_run - m_use);
+            float psum = 0.f;
+#pragma unroll
+            for (int step = 0; step < kSteps; ++step) {
+                pv[step] = fast_exp2(sc[step] - m_use);
+                psum += pv[step];
+            }
+            l_run = l_run * alpha + psum;
+            m_run = m_new;
+        };
+        // Stores p and the rescale into the warp's buffer `buf`; the caller's
+        // __syncwarp publishes them to the warp.
+        auto publish = [&](const float (&pv)[kSteps], float alpha, int buf) {
+            float* pb = pw + buf * (kKeysPerWarp * kGroup);
+            if ((g & 1) == 0) {
+#pragma unroll
+                for (int step = 0; step < kSteps; ++step) pb[(step * 4 + slot) * kGroup + hh] = pv[step];
+                if (slot == 0) aw[buf * kGroup + hh] = alpha;
+            }
+        };
+
+        // acc = acc * alpha + sum_k p_k * V_k over this warp's keys of tile t.
+        // In the split's last tile, rows past its keys may hold anything (even
+        // NaN): their probabilities are 0, and each lane zeroes the 8 bytes of
+        // those rows that it reads itself, so no other lane is involved.
+        auto pv_tile = [&](int t, int buf, bool last) {
+            uint8_t* vt = smem + ((ring0 + t) % kStages) * kStageBytes + kTileBytes;
+            if (last) {
+                const int nr = min(kTileKeys, cnt - t * kTileKeys) - c * kKeysPerWarp;
+#pragma unroll
+                for (int rr = 0; rr < kKeysPerWarp; ++rr)
+                    if (rr >= nr)
+                        *reinterpret_cast<uint2*>(vt + (c * kKeysPerWarp + rr) * kRowBytes + lane * 8) = make_uint2(0u, 0u);
+            }
+            const float* pb = pw + buf * (kKeysPerWarp * kGroup);
+            const float4 al = *reinterpret_cast<const float4*>(aw + buf * kGroup);
+            const float alv[4] = {al.x, al.y, al.z, al.w};
+#pragma unroll
+            for (int hq = 0; hq < kGroup; ++hq) {
+                acc0[hq] = __fmul2_rn(acc0[hq], f2(alv[hq]));
+                acc1[hq] = __fmul2_rn(acc1[hq], f2(alv[hq]));
+            }
+#pragma unroll
+            for (int rr = 0; rr < kKeysPerWarp; ++rr) {
+                const float4 p4 = *reinterpret_cast<const float4*>(pb + rr * kGroup);
+                const uint2 vv = *reinterpret_cast<const uint2*>(vt + (c * kKeysPerWarp + rr) * kRowBytes + lane * 8);
+                const float2 v0 = bf16x2_to_float2(vv.x), v1 = bf16x2_to_float2(vv.y);
+                const float pk[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+                for (int hq = 0; hq < kGroup; ++hq) {
+                    acc0[hq] = ffma2_bcast(pk[hq], v0, acc0[hq]);
+                    acc1[hq] = ffma2_bcast(pk[hq], v1, acc1[hq]);
+                }
+            }
+        };
+
+        // Software pipeline: one iteration computes the scores and the softmax of
+        // tile t and the P.V of tile t-1, with no branch or warp barrier between
+        // them, so that the two independent instruction streams interleave; the
+        // probabilities of tile t are stored after the P.V loads of tile t-1 (a
+        // different buffer) and published by one __syncwarp.
+        if (ok && n_tiles > 0) {
+            if (mbar_wait(&full[ring0 % kStages], (ring0 / kStages) & 1)) {
+                float sc[kSteps], pv[kSteps], alpha;
+                qk_tile(0, sc);
+                softmax_tile(sc, pv, alpha);
+                publish(pv, alpha, 0);
+                __syncwarp();
+            } else {
+                ok = false;
+            }
+        }
+        for (int t = 1; t < n_tiles && ok; ++t) {
+            if (!mbar_wait(&full[(ring0 + t) % kStages], ((ring0 + t) / kStages) & 1)) {
+                ok = false;
+                break;
+            }
+            float sc[kSteps], pv[kSteps], alpha;
+            qk_tile(t, sc);
+            softmax_tile(sc, pv, alpha);
+            pv_tile(t - 1, (t - 1) & 1, false);
+            publish(pv, alpha, t & 1);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[(ring0 + t - 1) % kStages]);
+        }
+        if (ok && n_tiles > 0) {
+            pv_tile(n_tiles - 1, (n_tiles - 1) & 1, true);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[(ring0 + n_tiles - 1) % kStages]);
+        }
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 8);
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 16);
+
+        // ---- merge the warps through the epilogue region, once every consumer
+        // has finished the previous item's epilogue; a timed-out wait in any
+        // warp ends the item loop after this item, for all of them.
+        const bool any_failed = named_barrier_or(1, kConsumerThreads, !ok);
+        {
+            float* mine = cb + c * kGroup * kPartialFloats;
+#pragma unroll
+            for (int hq = 0; hq < kGroup; ++hq)
+                *reinterpret_cast<float4*>(mine + hq * kPartialFloats + 4 * lane) =
+                    make_float4(acc0[hq].x, acc0[hq].y, acc1[hq].x, acc1[hq].y);
+            if (slot == 0 && (g & 1) == 0) {
+                mine[hh * kPartialFloats + 128] = m_run;
+                mine[hh * kPartialFloats + 129] = l_run;
+            }
+        }
+        named_barrier_sync(1, kConsumerThreads);
+        // Factors once per (warp, head): thread t < 44 owns warp t / 4, head t % 4.
+        if (tid < kConsumerWarps * kGroup) {
+            const int hq = tid & 3;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, cb[(w * kGroup + hq) * kPartialFloats + 128]);
+            const float* row = cb + tid * kPartialFloats;  // warp tid / 4, head tid % 4
+            const float f = exp2f(row[128] - (M == -INFINITY ? 0.f : M));
+            wf[tid] = f;
+            wl[tid] = row[129] * f;
+            if (tid < kGroup) wm[hq] = M;
+        }
+        named_barrier_sync(1, kConsumerThreads);
+        // Thread t < 128 merges head t / 32, dims 4 (t % 32) .. +3.
+        if (tid < kOutputs / 4) {
+            const int hq = tid >> 5, d0 = (tid & 31) * 4;
+            float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+            float L = 0.f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                const float f = wf[w * kGroup + hq];
+                const float4 x = *reinterpret_cast<const float4*>(cb + (w * kGroup + hq) * kPartialFloats + d0);
+                O = make_float4(fmaf(x.x, f, O.x), fmaf(x.y, f, O.y), fmaf(x.z, f, O.z), fmaf(x.w, f, O.w));
+                L += wl[w * kGroup + hq];
+            }
+            const float M = wm[hq];
+            if (n_split == 1) {
+                write_result4(direct, b, h * kGroup + hq, d0, O, M, L);
+            } else {
+                float* row = a.ws_partials + ((int64_t)lsplit * kNumKVHeads + h) * kGroup * kPartialFloats +
+                             hq * kPartialFloats;
+                *reinterpret_cast<float4*>(row + d0) = O;
+                if (d0 == 0) {
+                    row[128] = M;
+                    row[129] = L;
+                }
+            }
+        }
+        ring0 += n_tiles;
+        if (any_failed) {
+            ok = false;
+            break;
+        }
+    }
+    if (!ok && lane == 0) atomicOr(a.ws_status, kDevStatusTimeout);
+}
+
+// ---------------------------------------------------------------------------
 // Merge of a sequence's split partials: one CTA per (sequence, Q head), one
 // thread per dim.  Runs after decode_kernel (griddepcontrol.wait).
 // ---------------------------------------------------------------------------
@@ -1255,6 +1871,11 @@ cudaError_t decode_prepare(int device) {
         if (cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
             (void)cudaGetLastError();
     }
+    for (const void* f : {reinterpret_cast<const void*>(decode_queue_kernel<false>),
+                          reinterpret_cast<const void*>(decode_queue_kernel<true>)}) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kQueueSmemBytes);
+        if (e != cudaSuccess) return e;
+    }
     return cudaSuccess;
 }
 
@@ -1283,9 +1904,20 @@ cudaError_t launch_decode(const DecodeArgs& a, int total_splits, cudaStream_t st
     void* dargs[] = {const_cast<DecodeArgs*>(&a)};
     const void* kern = (a.flags & GQA_FLAG_K_ROTATED) ? reinterpret_cast<const void*>(decode_kernel<true>)
                                                        : reinterpret_cast<const void*>(decode_kernel<false>);
-    if (a.cluster > 0)  // single sequence, merged inside the clusters
+    cudaError_t e;
+    if (a.cluster > 0) {  // single sequence, merged inside the clusters
         return launch_pdl(kern, dim3(a.cluster, a.n_heads), dim3(kThreads), kSmemBytes, stream, dargs, a.cluster);
-    cudaError_t e = launch_pdl(kern, dim3(total_splits * a.n_heads), dim3(kThreads), kSmemBytes, stream, dargs);
+    } else if (a.ws_work != nullptr) {  // a batch: one CTA per SM works through the items
+        int dev = 0, sms = 0;
+        e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+        const void* qk = (a.flags & GQA_FLAG_K_ROTATED) ? reinterpret_cast<const void*>(decode_queue_kernel<true>)
+                                                         : reinterpret_cast<const void*>(decode_queue_kernel<false>);
+        e = launch_pdl(qk, dim3(std::min(a.n_items, sms)), dim3(kThreads), kQueueSmemBytes, stream, dargs);
+    } else {
+        e = launch_pdl(kern, dim3(total_splits * a.n_heads), dim3(kThreads), kSmemBytes, stream, dargs);
+    }
     // Done when every sequence had one split or the last split of each head merged.
     if (e != cudaSuccess || total_splits <= a.batch || a.ws_arrivals != nullptr) return e;
     MergeArgs m;

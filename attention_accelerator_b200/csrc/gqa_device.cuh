@@ -104,6 +104,9 @@ struct alignas(64) DecodeArgs {
     int world, rank;             // merged rows with the other ranks' exchange buffers (device array)
     int head0, n_heads;     // KV heads [head0, head0 + n_heads) only; the K/V maps then hold just those
                             // heads (map head index = h - head0).  0 and 8 for a whole call.
+    uint32_t* ws_work;      // non-null: a batch run by decode_queue_kernel, one CTA per SM taking the
+    int n_items;            // n_items (split, KV head) items from this queue (next item, CTAs done;
+                            // both zero between calls)
 };
 
 // Exchange buffer of the long-context split (one per rank, mapped by the others):
@@ -244,6 +247,20 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Named barrier that also returns whether any participating thread passed true.
+__device__ __forceinline__ bool named_barrier_or(int id, int threads, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %3, 0;\n\t"
+        "barrier.red.or.pred q, %1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(id), "r"(threads), "r"(v ? 1u : 0u)
+        : "memory");
+    return r != 0;
 }
 
 // Arrive on a named barrier without waiting (the producer side of a hand-off:

@@ -156,9 +156,10 @@ int gqa_validate(const gqa_params *p);
  * Bytes of device workspace a call needs (0 on invalid input).  `descs` is the
  * host copy of the batch's descriptors, or NULL with batch == 1 for a
  * single-sequence call described by p->seq_len / p->query_position.
- * The workspace's first 256 bytes (the device status word and the per-KV-head
- * arrival counters of the single-sequence split merge) must be zero when it is
- * allocated; every call leaves the counters zero again, and gqa_read_status
+ * The workspace's first 256 bytes (the device status word, the per-KV-head
+ * arrival counters of the single-sequence split merge and a batch's work-queue
+ * counters) must be zero when it is allocated; every call leaves the counters
+ * zero again, and gqa_read_status
  * clears the whole header after a timed-out wait.  The rest needs no
  * initialisation (every call writes its split partials before reading them).
  * Calls that share a workspace must be ordered (one stream).  With `descs`
