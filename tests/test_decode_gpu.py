@@ -334,7 +334,7 @@ def test_interleaved_split_counts_share_workspace(cuda_device):
 def test_config3_full_batch(cuda_device):
     """BASELINE config 3 at full size: the bench's 64 sequence lengths
     (U{512..8192}, 301,934 keys, K with per-channel outlier scales) in one
-    launch of 1088 CTAs plus the split merge, each sequence against the float64
+    launch of 1088 (split, KV head) items plus the split merge, each sequence against the float64
     oracle.  Bar: the reference's per-element rule on all 262,144 outputs with
     no exception (``assert_chunk_parity``, measured on B200: 0 beyond 64 ULP,
     worst 43 ULP on a near-zero output), <= 2 ULP on large outputs."""

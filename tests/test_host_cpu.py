@@ -157,8 +157,9 @@ def _host_plan(seq_len=None, seqs=None, sms=148):
 
 
 def test_host_planner_reproduces_the_grids_measured_on_b200():
-    """The split planner, run without a GPU for 148 SMs, gives the grids ncu recorded
-    on the B200 (8 CTAs per split): config 2 136 CTAs, config 4 144, config 3 1088."""
+    """The split planner, run without a GPU for 148 SMs, gives the splits ncu recorded
+    on the B200 (8 per split, one per KV head): config 2 136 CTAs, config 4 144, config 3
+    1088 (split, KV head) items (a batch runs them from a work queue on one CTA per SM)."""
     assert _host_plan(4096) == (17, 248)       # one head group of SMs left for the next call
     assert _host_plan(131072) == (18, 7288)
     seqs = [int(x) for x in np.random.default_rng(20260805).integers(512, 8193, size=64)]  # bench config 3
