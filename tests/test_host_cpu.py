@@ -373,8 +373,10 @@ def test_bench_reference_arm_json_line():
 
 
 def test_bench_output_check_counts_ulps_like_the_reference():
-    """bench.compare_outputs: BF16 code distance across zero, the 64-ULP count and
-    the bar on large outputs (<= 2 ULP where |x| >= 2^-10 of the row's largest)."""
+    """bench.compare_outputs: BF16 code distance across zero, the 64-ULP count, the
+    bar on large outputs (<= 2 ULP where |x| >= 2^-10 of the row's largest), and
+    cancellation residues (below 2^-18 of the row's largest, the two values within
+    2^-19 of it) counted apart from failures."""
     import torch
     import bench
     want = torch.zeros((2, 128), dtype=torch.bfloat16)
@@ -390,9 +392,17 @@ def test_bench_output_check_counts_ulps_like_the_reference():
     res = bench.compare_outputs(got, want, "x")
     assert not res["ok"] and res["max_ulp_large_outputs"] == 3
     got = want.clone()
-    got[1, 1] = -got[1, 1]                        # sign flip of a tiny value: far beyond 64 codes
+    got[1, 1] = -got[1, 1]                        # sign flip of a residue: far beyond 64 codes, 2^-19 apart
+    res = bench.compare_outputs(got, want, "x")
+    assert res["ok"] and res["beyond_64_ulp"] == 0 and res["residues_beyond_64_ulp"] == 1
+    got[1, 1] = 2.0 ** -14                        # a residue, but the values are 2^-16 of the row max apart
     res = bench.compare_outputs(got, want, "x")
     assert not res["ok"] and res["beyond_64_ulp"] == 1 and res["max_ulp_large_outputs"] == 0
+    want[1, 2] = 2.0 ** -12                       # not a residue (2^-14 of the row max)
+    got = want.clone()
+    got[1, 2] = -got[1, 2]
+    res = bench.compare_outputs(got, want, "x")
+    assert not res["ok"] and res["beyond_64_ulp"] == 1 and res["residues_beyond_64_ulp"] == 0
 
 
 def test_decode_heads_refuses_bad_head_ranges_before_any_gpu_work():
