@@ -854,7 +854,10 @@ def make_workload(name, device, rank, world, layout="position_major", chunk_batc
 
 # ---------------------------------------------------------------------------
 def timed_graph_run(torch, wl, steps, warmup, stream, dist_on):
-    """Capture one replay of every buffer set (and a remainder) as CUDA graphs; time K steps."""
+    """Capture the steps as CUDA graphs of up to 64 steps (a whole number of
+    passes over the rotating buffer sets, and a remainder) and time K steps.
+    Within a graph each kernel's set-up overlaps the previous kernel's tail
+    (programmatic dependent launch); a boundary between graph replays does not."""
     with torch.cuda.stream(stream):
         for i in range(max(warmup, 1)):
             wl.launch(i)
@@ -871,7 +874,7 @@ def timed_graph_run(torch, wl, steps, warmup, stream, dist_on):
             graphs[n] = g
         return graphs[n]
 
-    n = wl.sets
+    n = wl.sets * max(1, min(steps, 64) // wl.sets)
     if use_graphs:
         graph_of(n)
         if steps % n:
