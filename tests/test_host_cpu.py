@@ -86,7 +86,7 @@ def test_bench_traffic_applies_only_to_the_captured_launch():
     import bench
     assert bench.traffic_for("config4_decode_s131072", 536887296) == 541605632
     assert bench.traffic_for("config4_decode_s131072", 536887296 / 4) is None  # a rank's shard at N=4
-    assert bench.traffic_for("config3_ragged_b64", 1237770240) == 1260021760
+    assert bench.traffic_for("config3_ragged_b64", 1237770240) == 1257566976  # decode_queue_kernel
     assert bench.traffic_for("no_such_workload", 1.0) is None
 
 
