@@ -56,9 +56,9 @@ namespace gqa {
 
 namespace {
 
-// 11 consumer warps + 1 producer warp = 12 warps: the most warps the 160
-// registers a consumer thread needs allow (64K registers per SM; at 16 warps
-// the allocation would be 128).
+// 11 consumer warps + 1 producer warp = 12 warps: the most warps the 157
+// registers a consumer thread needs allow (160 allocated; 64K registers per
+// SM; at 16 warps the allocation would be 128).
 constexpr int kConsumerWarps = kDecodeConsumerWarps;
 constexpr int kKeysPerWarp = kDecodeKeysPerWarp;  // keys of one tile per warp
 constexpr int kTileKeys = kDecodeTileKeys;        // 88 keys per pipeline tile
